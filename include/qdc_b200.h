@@ -1,0 +1,195 @@
+/*
+ * qdc_b200.h -- C ABI of libqdc_b200.so, the B200 (sm_100a) implementation of
+ * QwenDecisionCore.jl's memory-bound per-layer row ops.
+ *
+ * Every entry point replaces one hook that the reference's CUDA extension
+ * overrides through Julia multiple dispatch; the hook is cited (file:line
+ * inside the QwenDecisionCore.jl project) beside each declaration.  The
+ * reference binds its GPU code with CUDA.jl `@cuda` launches; a Julia
+ * extension binds this library with `ccall`.
+ *
+ * Conventions
+ *  - Layouts are the reference's column-major Julia matrices seen row-major:
+ *    a Julia (width, tokens) Float32 matrix is `[tokens][width]` here.  Each
+ *    row operand carries a leading dimension `ld_*` in ELEMENTS.
+ *  - Device pointers are owned by the caller; the library never frees them.
+ *    `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *    stream-ordered and asynchronous unless stated otherwise.
+ *  - Every call returns a qdc_status.  Arguments are validated on the host
+ *    before anything is launched; on error nothing is launched and
+ *    qdc_last_error() describes the failure.  No kernel traps: an
+ *    out-of-vocabulary id that reaches the device raises a flag that
+ *    qdc_sync() reports as QDC_EBOUNDS.
+ *  - One context serves one host thread at a time (as the reference's
+ *    per-model workspace lock, ext/cuda_workspace.jl:48-69); different
+ *    contexts may be used concurrently.
+ *  - Float32 arithmetic follows the reference's CPU operation order
+ *    (src/backbone_cpu.jl) with separately rounded multiplies and adds;
+ *    bf16 storage follows src/safetensors.jl:28-30,38-42.
+ */
+#ifndef QDC_B200_H
+#define QDC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QDC_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define QDC_API __attribute__((visibility("default")))
+#else
+#define QDC_API
+#endif
+
+typedef enum qdc_status {
+    QDC_OK = 0,
+    QDC_EINVAL = 1,   /* bad shape, null/misaligned pointer, bad dtype */
+    QDC_EBOUNDS = 2,  /* token id outside the vocabulary */
+    QDC_ECUDA = 3,    /* a CUDA runtime call failed */
+    QDC_ENOMEM = 4,   /* workspace exhausted or device allocation failed */
+    QDC_EDEVICE = 5   /* device is not a compute capability 10.0 GPU */
+} qdc_status;
+
+typedef enum qdc_dtype {
+    QDC_F32 = 0,      /* Float32 storage */
+    QDC_BF16 = 1      /* bfloat16 storage (uint16 bits), Float32 math */
+} qdc_dtype;
+
+typedef struct qdc_ctx qdc_ctx;
+
+/* ---- library / context ---------------------------------------------------- */
+
+QDC_API int qdc_abi_version(void);
+QDC_API const char *qdc_status_string(int status);
+
+/* Create a context bound to CUDA device `device`: the owner of a forward's
+ * workspace arena and device error flag.  Replaces the per-model
+ * ForwardWorkspace of ext/cuda_workspace.jl:4-46. */
+QDC_API int qdc_init(int device, qdc_ctx **out);
+QDC_API int qdc_destroy(qdc_ctx *ctx);
+
+/* Text of the last failure on this context (or on this thread, ctx NULL). */
+QDC_API const char *qdc_last_error(const qdc_ctx *ctx);
+
+/* Synchronize `stream`, then report QDC_EBOUNDS (and clear the flag) if a
+ * kernel saw an out-of-vocabulary id since the last call.  Replaces the
+ * synchronize in native_forward_scope's `finally`, ext/cuda_workspace.jl:62-66. */
+QDC_API int qdc_sync(qdc_ctx *ctx, void *stream);
+
+/* ---- workspace arena -------------------------------------------------------
+ * Bump allocator over one device allocation per context, reused forward after
+ * forward.  Replaces the slot list `scratch(T, dims)` of
+ * ext/cuda_workspace.jl:71-87 and the cursor reset of :57-59. */
+
+/* Ensure capacity >= bytes.  Growing frees and reallocates the arena, which
+ * invalidates every pointer handed out before; it synchronizes the device. */
+QDC_API int qdc_ws_reserve(qdc_ctx *ctx, size_t bytes);
+/* Carve `bytes` (rounded up to `align`, a power of two >= 256 or 0 for 256). */
+QDC_API int qdc_ws_alloc(qdc_ctx *ctx, size_t bytes, size_t align, void **out);
+/* Current cursor, and pop back to a cursor taken earlier. */
+QDC_API int qdc_ws_mark(qdc_ctx *ctx, size_t *mark);
+QDC_API int qdc_ws_release(qdc_ctx *ctx, size_t mark);
+/* cursor = 0: the start of a forward (native_forward_scope, :57-58). */
+QDC_API int qdc_ws_reset(qdc_ctx *ctx);
+QDC_API int qdc_ws_stats(const qdc_ctx *ctx, size_t *used, size_t *capacity,
+                 size_t *high_water);
+
+/* ---- host tables -------------------------------------------------------------
+ * RoPE cos/sin tables exactly as src/backbone_cpu.jl:90-105 builds them:
+ * freq_j = inv(theta^(Float32(2j)/Float32(rotary))), angle = freq_j*Float32(p)
+ * (one Float32 multiply), cos/sin of the Float32 angle rounded to Float32.
+ * Fills host arrays [n][rotary/2].  Pure host code; no context needed. */
+QDC_API int qdc_rope_table(float theta, int rotary, int64_t n, float *cos_host,
+                   float *sin_host);
+
+/* ---- per-layer row kernels ----------------------------------------------- */
+
+/* Token-embedding gather fused with an optional residual add and the input
+ * RMSNorm:  r_t = E[ids_t] (+ add_t);  y_t = rms(r_t) * (1+g | g).
+ *   table   [vocab][hidden] (Julia (hidden, vocab)), dtype storage
+ *   ids     HOST int32[n], 0-based; validated before launch (QDC_EBOUNDS,
+ *           src/backbone.jl:417-418) and staged into the context workspace
+ *           (the reference stages them the same way, ext/cuda_workspace.jl:333-334)
+ *   add     optional [n][hidden] residual (NULL: none)
+ *   out_x   optional [n][hidden] r (NULL: not stored); with gamma NULL the
+ *           call is the plain gather of ext/cuda_workspace.jl:317-344
+ *   out_y   [n][hidden] normalized output (NULL allowed only if gamma NULL)
+ *   gamma   Float32[hidden] (centered: applied as 1+g, src/backbone_cpu.jl:346)
+ * Replaces native_gather (src/backbone.jl:55-64, ext/cuda_workspace.jl:330-344)
+ * followed by the first layer's native_rms (src/backbone.jl:364). */
+QDC_API int qdc_gather_rms(qdc_ctx *ctx, void *out_x, void *out_y, const void *table,
+                   const int32_t *ids, const void *add, const float *gamma,
+                   float eps, int centered, int64_t n, int64_t hidden,
+                   int64_t vocab, int dtype, void *stream);
+
+/* As qdc_gather_rms with DEVICE ids (for graph capture / device-resident
+ * batches).  Out-of-range ids are not read: their rows are filled with NaN
+ * and the context flag is raised (QDC_EBOUNDS from the next qdc_sync). */
+QDC_API int qdc_gather_rms_device_ids(qdc_ctx *ctx, void *out_x, void *out_y,
+                              const void *table, const int32_t *ids_dev,
+                              const void *add, const float *gamma, float eps,
+                              int centered, int64_t n, int64_t hidden,
+                              int64_t vocab, int dtype, void *stream);
+
+/* Residual add + RMSNorm:  r = x + m (m NULL: r = x);  y = rms(r)*(1+g | g);
+ * r stored when out_r != NULL.  One kernel covers
+ *  - native_rms (src/backbone.jl:200-204, ext/cuda_workspace.jl:139-170):
+ *    m NULL, out_r NULL -- the input norm and the final norm;
+ *  - native_residual_rms (src/backbone.jl:347-350, src/backbone_cpu.jl:321-328,
+ *    ext/cuda_workspace.jl:179-209): the post-attention norm;
+ *  - native_residual_add! (src/backbone.jl:358-361) fused with the NEXT
+ *    layer's input norm (or with the final norm, src/backbone.jl:410).
+ * out_r may alias x (in-place residual stream); out_y must not alias x/m. */
+QDC_API int qdc_residual_rms(qdc_ctx *ctx, void *out_r, void *out_y, const void *x,
+                     const void *m, const float *gamma, float eps,
+                     int centered, int64_t rows, int64_t width, int64_t ld_x,
+                     int64_t ld_m, int64_t ld_r, int64_t ld_y, int dtype,
+                     void *stream);
+
+/* Per-head q/k RMSNorm (centered gamma) + rotate-half partial RoPE on the
+ * first `rotary` dims; dims >= rotary pass through.  Input head h of token
+ * t starts at in + t*in_tok + h*in_head (q straight from the packed [q;gate]
+ * projection: in_tok = heads*2*dim, in_head = 2*dim, src/backbone.jl:226-227).
+ * Output dense [tokens][heads][dim].  Position of token t:
+ * pos_offset + t % seq_len (seq_len <= 0: t), which must be < table_rows.
+ * cos_tab/sin_tab: device [table_rows][rotary/2] from qdc_rope_table.
+ * Replaces native_rms + native_rope in full_attention (src/backbone.jl:
+ * 206-235; CPU src/backbone_cpu.jl:113-136; CUDA prepare_head_kernel!
+ * ext/cuda_attention.jl:1-45).  K is written once per kv head, not
+ * expanded per query head. */
+QDC_API int qdc_qk_norm_rope(qdc_ctx *ctx, float *out, const float *in,
+                     int64_t tokens, int heads, int dim, int64_t in_tok,
+                     int64_t in_head, const float *gamma, float eps,
+                     int rotary, const float *cos_tab, const float *sin_tab,
+                     int64_t table_rows, int64_t pos_offset, int64_t seq_len,
+                     void *stream);
+
+/* Gated RMSNorm of the Gated DeltaNet output:  y = ((o*s)*g)*silu(z),
+ * uncentered gamma (src/backbone.jl:339-341, src/backbone_cpu.jl:750-755).
+ * o head h of row t at o + t*o_ld + h*dim; z at z + t*z_ld + z_off + h*dim
+ * (z read in place from the packed projection, ext/cuda_delta.jl:232-241);
+ * y at out + t*out_ld + h*dim.  Replaces rms_gate_kernel!
+ * (ext/cuda_delta.jl:99-116). */
+QDC_API int qdc_gated_rms(qdc_ctx *ctx, float *out, const float *o, const float *z,
+                  int64_t rows, int heads, int dim, int64_t o_ld, int64_t z_ld,
+                  int64_t z_off, int64_t out_ld, const float *gamma,
+                  float eps, void *stream);
+
+/* SwiGLU gate:  h = silu(g) * u  (src/backbone.jl:196-197,352-355).
+ * g/u rows at g + t*ld_g, u + t*ld_u (the packed [gate;up] projection of
+ * ext/cuda_mlp.jl:63-71 is g = P, u = P + width, ld = 2*width).  Writes
+ * Float32 out_f32 and/or bf16 out_bf16 (either may be NULL, not both), both
+ * with leading dimension ld_out.  Replaces mlp_gate_kernel!
+ * (ext/cuda_mlp.jl:49-61) and native_mlp_gate! (src/backbone.jl:352-355). */
+QDC_API int qdc_swiglu(qdc_ctx *ctx, float *out_f32, uint16_t *out_bf16,
+               const float *g, const float *u, int64_t rows, int64_t width,
+               int64_t ld_g, int64_t ld_u, int64_t ld_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QDC_B200_H */

@@ -1,0 +1,561 @@
+// qdc_b200.cu -- C ABI of libqdc_b200.so (declared in include/qdc_b200.h).
+//
+// Host side of the library: context + workspace arena, argument validation
+// (every check happens before anything is launched), launch-shape selection
+// (vector kernel specialised on the row width when every operand is 16-byte
+// aligned, scalar kernel otherwise) and persistent grid sizing from the
+// occupancy calculator.
+#include "qdc_b200.h"
+#include "qdc_kernels.cuh"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+struct qdc_ctx {
+    int device = -1;
+    int sm_count = 0;
+    std::string err;
+    // workspace arena
+    char* arena = nullptr;
+    size_t capacity = 0, cursor = 0, high_water = 0;
+    // device error flag (one int) + staging for host ids
+    int* flag = nullptr;
+    int32_t* ids_stage = nullptr;
+    size_t ids_capacity = 0;
+    cudaEvent_t ids_done = nullptr;  // last kernel that read ids_stage
+};
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(qdc_ctx* ctx, int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    t_err = buf;
+    return status;
+}
+
+int cuda_fail(qdc_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, QDC_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define QDC_CUDA(ctx, call)                                       \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return cuda_fail((ctx), e_, #call); \
+    } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Switches to the context's device for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    bool switched = false;
+    cudaError_t status = cudaSuccess;
+    explicit DeviceGuard(int dev) {
+        status = cudaGetDevice(&prev);
+        if (status == cudaSuccess && prev != dev) {
+            status = cudaSetDevice(dev);
+            switched = status == cudaSuccess;
+        }
+    }
+    ~DeviceGuard() {
+        if (switched) cudaSetDevice(prev);
+    }
+};
+
+// Blocks per SM that keep one instance of `kernel` resident, cached per
+// (kernel, device).
+int resident_blocks(const void* kernel, int device, int threads) {
+    static std::mutex mu;
+    static std::unordered_map<uint64_t, int> cache;
+    const uint64_t key = reinterpret_cast<uint64_t>(kernel) ^ (uint64_t(device) << 56);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n < 1)
+        n = 1;
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = n;
+    return n;
+}
+
+// Persistent grid: enough CTAs for the work, at most one full wave.
+int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units) {
+    const int64_t wanted = (units + work_per_block_units - 1) / work_per_block_units;
+    const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, qdc::kThreads);
+    int64_t g = wanted < cap ? wanted : cap;
+    return int(g < 1 ? 1 : g);
+}
+
+template <typename Kernel, typename Args>
+int launch(qdc_ctx* ctx, Kernel kernel, int grid, const Args& args, void* stream, const char* name) {
+    kernel<<<grid, qdc::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(args);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch %s: %s", name, cudaGetErrorString(e));
+    return QDC_OK;
+}
+
+// ---------------------------------------------------------------- row ops
+
+template <typename T>
+using RowKernel = void (*)(qdc::RowArgs);
+
+template <typename T>
+RowKernel<T> row_vec_kernel(int64_t chunks);
+
+template <>
+RowKernel<float> row_vec_kernel<float>(int64_t chunks) {
+    switch (chunks) {
+        case 1: return qdc::row_rms_vec<float, 1>;
+        case 2: return qdc::row_rms_vec<float, 2>;
+        case 3: return qdc::row_rms_vec<float, 3>;
+        case 4: return qdc::row_rms_vec<float, 4>;
+        case 6: return qdc::row_rms_vec<float, 6>;
+        case 8: return qdc::row_rms_vec<float, 8>;
+        case 12: return qdc::row_rms_vec<float, 12>;
+        case 16: return qdc::row_rms_vec<float, 16>;
+        default: return nullptr;
+    }
+}
+
+template <>
+RowKernel<uint16_t> row_vec_kernel<uint16_t>(int64_t chunks) {
+    switch (chunks) {
+        case 1: return qdc::row_rms_vec<uint16_t, 1>;
+        case 2: return qdc::row_rms_vec<uint16_t, 2>;
+        case 3: return qdc::row_rms_vec<uint16_t, 3>;
+        case 4: return qdc::row_rms_vec<uint16_t, 4>;
+        case 6: return qdc::row_rms_vec<uint16_t, 6>;
+        case 8: return qdc::row_rms_vec<uint16_t, 8>;
+        case 12: return qdc::row_rms_vec<uint16_t, 12>;
+        case 16: return qdc::row_rms_vec<uint16_t, 16>;
+        default: return nullptr;
+    }
+}
+
+template <typename T>
+int launch_rows(qdc_ctx* ctx, const qdc::RowArgs& a, void* stream) {
+    if (a.rows == 0) return QDC_OK;
+    constexpr int64_t N = 16 / sizeof(T);
+    const int64_t e = sizeof(T);
+    bool vec = a.width % (32 * N) == 0 && aligned16(a.x) && aligned16(a.out_y) &&
+               (a.out_r == nullptr || aligned16(a.out_r)) && (a.m == nullptr || aligned16(a.m)) &&
+               (a.ld_x * e) % 16 == 0 && (a.ld_y * e) % 16 == 0 &&
+               (a.out_r == nullptr || (a.ld_r * e) % 16 == 0) &&
+               (a.m == nullptr || (a.ld_m * e) % 16 == 0);
+    RowKernel<T> k = vec ? row_vec_kernel<T>(a.width / (32 * N)) : nullptr;
+    if (k == nullptr) k = qdc::row_rms_generic<T>;
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, a.rows);
+    return launch(ctx, k, grid, a, stream, "row_rms");
+}
+
+int check_ctx(qdc_ctx* ctx) {
+    if (ctx == nullptr) return fail(nullptr, QDC_EINVAL, "context is NULL");
+    return QDC_OK;
+}
+
+int row_common(qdc_ctx* ctx, qdc::RowArgs& a, int dtype, void* stream) {
+    if (dtype != QDC_F32 && dtype != QDC_BF16) return fail(ctx, QDC_EINVAL, "unknown dtype %d", dtype);
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    return dtype == QDC_F32 ? launch_rows<float>(ctx, a, stream) : launch_rows<uint16_t>(ctx, a, stream);
+}
+
+int gather_checks(qdc_ctx* ctx, const void* out_x, const void* out_y, const void* table,
+                  const float* gamma, int64_t n, int64_t hidden, int64_t vocab) {
+    if (n < 0 || hidden < 1 || vocab < 1)
+        return fail(ctx, QDC_EINVAL, "bad sizes n=%lld hidden=%lld vocab=%lld", (long long)n,
+                    (long long)hidden, (long long)vocab);
+    if (table == nullptr) return fail(ctx, QDC_EINVAL, "table is NULL");
+    if (gamma == nullptr && out_y != nullptr)
+        return fail(ctx, QDC_EINVAL, "out_y given without gamma");
+    if (gamma != nullptr && out_y == nullptr) return fail(ctx, QDC_EINVAL, "gamma given without out_y");
+    if (out_x == nullptr && out_y == nullptr) return fail(ctx, QDC_EINVAL, "no output requested");
+    return QDC_OK;
+}
+
+}  // namespace
+
+// ====================================================================== ABI
+
+extern "C" {
+
+int qdc_abi_version(void) { return QDC_B200_ABI_VERSION; }
+
+const char* qdc_status_string(int status) {
+    switch (status) {
+        case QDC_OK: return "ok";
+        case QDC_EINVAL: return "invalid argument";
+        case QDC_EBOUNDS: return "token id outside the vocabulary";
+        case QDC_ECUDA: return "CUDA error";
+        case QDC_ENOMEM: return "out of memory";
+        case QDC_EDEVICE: return "unsupported device";
+        default: return "unknown status";
+    }
+}
+
+const char* qdc_last_error(const qdc_ctx* ctx) { return ctx ? ctx->err.c_str() : t_err.c_str(); }
+
+int qdc_init(int device, qdc_ctx** out) {
+    if (out == nullptr) return fail(nullptr, QDC_EINVAL, "out is NULL");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceCount");
+    if (device < 0 || device >= count)
+        return fail(nullptr, QDC_EINVAL, "device %d out of range (%d devices)", device, count);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(nullptr, QDC_EDEVICE, "device %d is sm_%d%d; libqdc_b200 is built for sm_100a",
+                    device, prop.major, prop.minor);
+    qdc_ctx* ctx = new qdc_ctx();
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    DeviceGuard guard(device);
+    if (guard.status != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(nullptr, guard.status, "cudaSetDevice");
+    }
+    e = cudaMalloc(&ctx->flag, 256);
+    if (e == cudaSuccess) e = cudaMemset(ctx->flag, 0, 256);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ids_done, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        if (ctx->flag) cudaFree(ctx->flag);
+        delete ctx;
+        return cuda_fail(nullptr, e, "context setup");
+    }
+    *out = ctx;
+    return QDC_OK;
+}
+
+int qdc_destroy(qdc_ctx* ctx) {
+    if (ctx == nullptr) return QDC_OK;
+    {
+        DeviceGuard guard(ctx->device);
+        cudaDeviceSynchronize();
+        if (ctx->arena) cudaFree(ctx->arena);
+        if (ctx->flag) cudaFree(ctx->flag);
+        if (ctx->ids_stage) cudaFree(ctx->ids_stage);
+        if (ctx->ids_done) cudaEventDestroy(ctx->ids_done);
+    }
+    delete ctx;
+    return QDC_OK;
+}
+
+int qdc_sync(qdc_ctx* ctx, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int flag = 0;
+    QDC_CUDA(ctx, cudaMemcpyAsync(&flag, ctx->flag, sizeof flag, cudaMemcpyDeviceToHost, st));
+    QDC_CUDA(ctx, cudaStreamSynchronize(st));
+    if (flag) {
+        QDC_CUDA(ctx, cudaMemsetAsync(ctx->flag, 0, sizeof(int), st));
+        QDC_CUDA(ctx, cudaStreamSynchronize(st));
+        return fail(ctx, QDC_EBOUNDS, "Token ID is outside the vocabulary.");
+    }
+    return QDC_OK;
+}
+
+// ------------------------------------------------------------- workspace
+
+int qdc_ws_reserve(qdc_ctx* ctx, size_t bytes) {
+    if (int s = check_ctx(ctx)) return s;
+    if (bytes <= ctx->capacity) return QDC_OK;
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    const size_t granule = size_t(2) << 20;
+    const size_t cap = (bytes + granule - 1) / granule * granule;
+    QDC_CUDA(ctx, cudaDeviceSynchronize());
+    if (ctx->arena) cudaFree(ctx->arena);
+    ctx->arena = nullptr;
+    ctx->capacity = ctx->cursor = 0;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, cap);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, QDC_ENOMEM, "workspace of %zu bytes: %s", cap, cudaGetErrorString(e));
+    }
+    ctx->arena = static_cast<char*>(p);
+    ctx->capacity = cap;
+    return QDC_OK;
+}
+
+int qdc_ws_alloc(qdc_ctx* ctx, size_t bytes, size_t align, void** out) {
+    if (int s = check_ctx(ctx)) return s;
+    if (out == nullptr) return fail(ctx, QDC_EINVAL, "out is NULL");
+    *out = nullptr;
+    if (align == 0) align = 256;
+    if (align < 256 || (align & (align - 1)) != 0)
+        return fail(ctx, QDC_EINVAL, "alignment %zu is not a power of two >= 256", align);
+    const size_t start = (ctx->cursor + align - 1) & ~(align - 1);
+    if (start > ctx->capacity || bytes > ctx->capacity - start)
+        return fail(ctx, QDC_ENOMEM, "workspace exhausted: %zu bytes at %zu of %zu", bytes, start,
+                    ctx->capacity);
+    *out = ctx->arena + start;
+    ctx->cursor = start + bytes;
+    if (ctx->cursor > ctx->high_water) ctx->high_water = ctx->cursor;
+    return QDC_OK;
+}
+
+int qdc_ws_mark(qdc_ctx* ctx, size_t* mark) {
+    if (int s = check_ctx(ctx)) return s;
+    if (mark == nullptr) return fail(ctx, QDC_EINVAL, "mark is NULL");
+    *mark = ctx->cursor;
+    return QDC_OK;
+}
+
+int qdc_ws_release(qdc_ctx* ctx, size_t mark) {
+    if (int s = check_ctx(ctx)) return s;
+    if (mark > ctx->cursor) return fail(ctx, QDC_EINVAL, "mark %zu is past the cursor %zu", mark, ctx->cursor);
+    ctx->cursor = mark;
+    return QDC_OK;
+}
+
+int qdc_ws_reset(qdc_ctx* ctx) {
+    if (int s = check_ctx(ctx)) return s;
+    ctx->cursor = 0;
+    return QDC_OK;
+}
+
+int qdc_ws_stats(const qdc_ctx* ctx, size_t* used, size_t* capacity, size_t* high_water) {
+    if (ctx == nullptr) return fail(nullptr, QDC_EINVAL, "context is NULL");
+    if (used) *used = ctx->cursor;
+    if (capacity) *capacity = ctx->capacity;
+    if (high_water) *high_water = ctx->high_water;
+    return QDC_OK;
+}
+
+// ------------------------------------------------------------ RoPE tables
+
+int qdc_rope_table(float theta, int rotary, int64_t n, float* cos_host, float* sin_host) {
+    if (rotary < 0 || (rotary & 1) || n < 0)
+        return fail(nullptr, QDC_EINVAL, "bad rotary=%d n=%lld", rotary, (long long)n);
+    const int half = rotary / 2;
+    if (half > 0 && n > 0 && (cos_host == nullptr || sin_host == nullptr))
+        return fail(nullptr, QDC_EINVAL, "table pointers are NULL");
+    if (!(theta > 0.0f) || !std::isfinite(theta)) return fail(nullptr, QDC_EINVAL, "theta must be positive");
+    for (int j = 0; j < half; ++j) {
+        // Float32.(0:2:(r-1)) ./ Float32(r): one Float32 division
+        volatile float exponent = float(2 * j) / float(rotary);
+        // Float32 ^ Float32: evaluated in double, rounded once
+        volatile float power = float(std::pow(double(theta), double(exponent)));
+        volatile float freq = 1.0f / power;
+        for (int64_t p = 0; p < n; ++p) {
+            volatile float angle = freq * float(p);  // one Float32 multiply
+            cos_host[p * half + j] = float(std::cos(double(angle)));
+            sin_host[p * half + j] = float(std::sin(double(angle)));
+        }
+    }
+    return QDC_OK;
+}
+
+// ------------------------------------------------------------ row kernels
+
+int qdc_residual_rms(qdc_ctx* ctx, void* out_r, void* out_y, const void* x, const void* m,
+                     const float* gamma, float eps, int centered, int64_t rows, int64_t width,
+                     int64_t ld_x, int64_t ld_m, int64_t ld_r, int64_t ld_y, int dtype, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (rows < 0 || width < 1) return fail(ctx, QDC_EINVAL, "bad sizes rows=%lld width=%lld", (long long)rows, (long long)width);
+    if (x == nullptr || out_y == nullptr || gamma == nullptr)
+        return fail(ctx, QDC_EINVAL, "x, out_y and gamma are required");
+    if (ld_x < width || ld_y < width || (m && ld_m < width) || (out_r && ld_r < width))
+        return fail(ctx, QDC_EINVAL, "a leading dimension is smaller than the width");
+    if (out_y == x || (m && out_y == m)) return fail(ctx, QDC_EINVAL, "out_y must not alias x or m");
+    if (out_r && out_r == x && ld_r != ld_x) return fail(ctx, QDC_EINVAL, "in-place r needs ld_r == ld_x");
+    qdc::RowArgs a{out_r, out_y, x, m, gamma, nullptr, ctx->flag, eps, centered ? 1 : 0,
+                   rows, width, ld_x, m ? ld_m : width, out_r ? ld_r : width, ld_y, 0};
+    return row_common(ctx, a, dtype, stream);
+}
+
+int qdc_gather_rms_device_ids(qdc_ctx* ctx, void* out_x, void* out_y, const void* table,
+                              const int32_t* ids_dev, const void* add, const float* gamma, float eps,
+                              int centered, int64_t n, int64_t hidden, int64_t vocab, int dtype,
+                              void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (int s = gather_checks(ctx, out_x, out_y, table, gamma, n, hidden, vocab)) return s;
+    if (n > 0 && ids_dev == nullptr) return fail(ctx, QDC_EINVAL, "ids are NULL");
+    // Plain gather (gamma and out_y NULL): the row kernel stores r only.
+    qdc::RowArgs a{out_x, out_y, table, add, gamma, ids_dev, ctx->flag, eps, centered ? 1 : 0,
+                   n, hidden, hidden, hidden, hidden, hidden, vocab};
+    if (dtype != QDC_F32 && dtype != QDC_BF16) return fail(ctx, QDC_EINVAL, "unknown dtype %d", dtype);
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    if (n == 0) return QDC_OK;
+    return dtype == QDC_F32 ? launch_rows<float>(ctx, a, stream) : launch_rows<uint16_t>(ctx, a, stream);
+}
+
+int qdc_gather_rms(qdc_ctx* ctx, void* out_x, void* out_y, const void* table, const int32_t* ids,
+                   const void* add, const float* gamma, float eps, int centered, int64_t n,
+                   int64_t hidden, int64_t vocab, int dtype, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (int s = gather_checks(ctx, out_x, out_y, table, gamma, n, hidden, vocab)) return s;
+    if (n > 0 && ids == nullptr) return fail(ctx, QDC_EINVAL, "ids are NULL");
+    for (int64_t t = 0; t < n; ++t)  // check_sequence, src/backbone.jl:417-418
+        if (ids[t] < 0 || int64_t(ids[t]) >= vocab)
+            return fail(ctx, QDC_EBOUNDS, "Token ID is outside the vocabulary.");
+    if (n == 0) return QDC_OK;
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t bytes = size_t(n) * sizeof(int32_t);
+    if (bytes > ctx->ids_capacity) {
+        QDC_CUDA(ctx, cudaDeviceSynchronize());
+        if (ctx->ids_stage) cudaFree(ctx->ids_stage);
+        ctx->ids_stage = nullptr;
+        ctx->ids_capacity = 0;
+        const size_t cap = bytes < 65536 ? 65536 : bytes;
+        cudaError_t e = cudaMalloc(&ctx->ids_stage, cap);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, QDC_ENOMEM, "id staging buffer: %s", cudaGetErrorString(e));
+        }
+        ctx->ids_capacity = cap;
+    }
+    // The previous reader of the staging buffer may run on another stream.
+    QDC_CUDA(ctx, cudaStreamWaitEvent(st, ctx->ids_done, 0));
+    QDC_CUDA(ctx, cudaMemcpyAsync(ctx->ids_stage, ids, bytes, cudaMemcpyHostToDevice, st));
+    int s = qdc_gather_rms_device_ids(ctx, out_x, out_y, table, ctx->ids_stage, add, gamma, eps,
+                                      centered, n, hidden, vocab, dtype, stream);
+    if (s != QDC_OK) return s;
+    QDC_CUDA(ctx, cudaEventRecord(ctx->ids_done, st));
+    return QDC_OK;
+}
+
+}  // extern "C"
+
+// ----------------------------------------------------------- head kernels
+
+namespace {
+
+using HeadKernel = void (*)(qdc::HeadArgs);
+
+template <bool GATED>
+HeadKernel head_vec_kernel(int dim, int* lpu) {
+    switch (dim) {
+        case 32: *lpu = 8; return qdc::head_norm_vec<8, 1, 4, GATED>;
+        case 64: *lpu = 16; return qdc::head_norm_vec<16, 1, 4, GATED>;
+        case 128: *lpu = 32; return qdc::head_norm_vec<32, 1, 4, GATED>;
+        case 256: *lpu = 32; return qdc::head_norm_vec<32, 2, 2, GATED>;
+        case 512: *lpu = 32; return qdc::head_norm_vec<32, 4, 1, GATED>;
+        default: return nullptr;
+    }
+}
+
+template <bool GATED>
+int launch_heads(qdc_ctx* ctx, const qdc::HeadArgs& a, bool vec_ok, void* stream, const char* name) {
+    if (a.units == 0) return QDC_OK;
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    int lpu = 32;
+    HeadKernel k = vec_ok ? head_vec_kernel<GATED>(a.dim, &lpu) : nullptr;
+    if (k != nullptr && !GATED && a.rotary > 4 * lpu) k = nullptr;  // rotary must lie in chunk 0
+    int64_t units_per_block;
+    if (k == nullptr) {
+        k = qdc::head_norm_generic<GATED>;
+        units_per_block = qdc::kThreads / 32;
+    } else {
+        const int unroll = a.dim == 256 ? 2 : (a.dim == 512 ? 1 : 4);
+        units_per_block = int64_t(qdc::kThreads / 32) * (32 / lpu) * unroll;
+    }
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), units_per_block, a.units);
+    return launch(ctx, k, grid, a, stream, name);
+}
+
+}  // namespace
+
+extern "C" {
+
+int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, int heads, int dim,
+                     int64_t in_tok, int64_t in_head, const float* gamma, float eps, int rotary,
+                     const float* cos_tab, const float* sin_tab, int64_t table_rows, int64_t pos_offset,
+                     int64_t seq_len, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (tokens < 0 || heads < 1 || dim < 1 || dim > 8192)
+        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d dim=%d", (long long)tokens, heads, dim);
+    if (rotary < 0 || (rotary & 1) || rotary > dim)
+        return fail(ctx, QDC_EINVAL, "rotary=%d must be even and <= dim=%d", rotary, dim);
+    if (out == nullptr || in == nullptr || gamma == nullptr)
+        return fail(ctx, QDC_EINVAL, "out, in and gamma are required");
+    if (in_tok < 0 || in_head < 0) return fail(ctx, QDC_EINVAL, "negative stride");
+    if (pos_offset < 0) return fail(ctx, QDC_EINVAL, "negative position offset");
+    if (rotary > 0 && tokens > 0) {
+        if (cos_tab == nullptr || sin_tab == nullptr) return fail(ctx, QDC_EINVAL, "RoPE tables are NULL");
+        const int64_t span = seq_len > 0 ? (tokens < seq_len ? tokens : seq_len) : tokens;
+        if (pos_offset + span - 1 >= table_rows)
+            return fail(ctx, QDC_EINVAL, "position %lld beyond the %lld-row RoPE table",
+                        (long long)(pos_offset + span - 1), (long long)table_rows);
+    }
+    const int half = rotary / 2;
+    bool vec = aligned16(out) && aligned16(in) && in_tok % 4 == 0 && in_head % 4 == 0 &&
+               (rotary == 0 || (half % 4 == 0 && aligned16(cos_tab) && aligned16(sin_tab)));
+    qdc::HeadArgs a{out, in, nullptr, gamma, cos_tab, sin_tab, eps, heads, dim, rotary,
+                    tokens * heads, in_tok, in_head, 0, 0, int64_t(heads) * dim, pos_offset, seq_len};
+    return launch_heads<false>(ctx, a, vec, stream, "qk_norm_rope");
+}
+
+int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int64_t rows, int heads,
+                  int dim, int64_t o_ld, int64_t z_ld, int64_t z_off, int64_t out_ld, const float* gamma,
+                  float eps, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (rows < 0 || heads < 1 || dim < 1)
+        return fail(ctx, QDC_EINVAL, "bad sizes rows=%lld heads=%d dim=%d", (long long)rows, heads, dim);
+    if (out == nullptr || o == nullptr || z == nullptr || gamma == nullptr)
+        return fail(ctx, QDC_EINVAL, "out, o, z and gamma are required");
+    const int64_t row_width = int64_t(heads) * dim;
+    if (o_ld < row_width || out_ld < row_width || z_off < 0 || z_ld < z_off + row_width)
+        return fail(ctx, QDC_EINVAL, "leading dimensions too small for heads*dim=%lld", (long long)row_width);
+    bool vec = aligned16(out) && aligned16(o) && aligned16(z) && o_ld % 4 == 0 && z_ld % 4 == 0 &&
+               z_off % 4 == 0 && out_ld % 4 == 0;
+    qdc::HeadArgs a{out, o, z, gamma, nullptr, nullptr, eps, heads, dim, 0,
+                    rows * heads, o_ld, dim, z_ld, z_off, out_ld, 0, 0};
+    return launch_heads<true>(ctx, a, vec, stream, "gated_rms");
+}
+
+// ------------------------------------------------------------------ SwiGLU
+
+int qdc_swiglu(qdc_ctx* ctx, float* out_f32, uint16_t* out_bf16, const float* g, const float* u,
+               int64_t rows, int64_t width, int64_t ld_g, int64_t ld_u, int64_t ld_out, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (rows < 0 || width < 1) return fail(ctx, QDC_EINVAL, "bad sizes rows=%lld width=%lld", (long long)rows, (long long)width);
+    if (g == nullptr || u == nullptr) return fail(ctx, QDC_EINVAL, "g and u are required");
+    if (out_f32 == nullptr && out_bf16 == nullptr) return fail(ctx, QDC_EINVAL, "no output requested");
+    if (ld_g < width || ld_u < width || ld_out < width)
+        return fail(ctx, QDC_EINVAL, "a leading dimension is smaller than the width");
+    if (rows == 0) return QDC_OK;
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    qdc::SwigluArgs a{out_f32, out_bf16, g, u, rows, width, ld_g, ld_u, ld_out};
+    const bool vec = width % 4 == 0 && ld_g % 4 == 0 && ld_u % 4 == 0 && ld_out % 4 == 0 &&
+                     aligned16(g) && aligned16(u) && (out_f32 == nullptr || aligned16(out_f32)) &&
+                     (out_bf16 == nullptr || (reinterpret_cast<uintptr_t>(out_bf16) & 7u) == 0);
+    void (*k)(qdc::SwigluArgs) = qdc::swiglu_generic;
+    if (vec) {
+        if (out_f32 && out_bf16) k = qdc::swiglu_vec<true, true>;
+        else if (out_f32) k = qdc::swiglu_vec<true, false>;
+        else k = qdc::swiglu_vec<false, true>;
+    }
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, rows);
+    return launch(ctx, k, grid, a, stream, "swiglu");
+}
+
+}  // extern "C"

@@ -1,0 +1,520 @@
+// qdc_kernels.cuh -- sm_100a kernels for QwenDecisionCore.jl's per-layer row ops.
+//
+// All of these ops stream rows through HBM once: no dense contraction, so no
+// tensor cores.  The design that follows from that:
+//  * one warp per row (or per head segment of a row), persistent grid sized
+//    from the occupancy calculator x 148 SMs, rows handed out grid-stride;
+//  * every load of a row is issued before any arithmetic (16-byte
+//    ld.global.nc per lane, the whole row in flight), so a warp keeps
+//    4-8 KB outstanding and ~20-30 resident warps per SM cover HBM latency;
+//  * the row lives in registers between the reduction and the write-back,
+//    so x (and m) are read exactly once -- the reference CUDA kernels read
+//    them twice (ext/cuda_workspace.jl:139-194);
+//  * gamma (and 1+gamma) is staged once per CTA in shared memory;
+//  * reductions are warp shuffles; RoPE partners are exchanged by shuffle
+//    instead of being re-read from global (ext/cuda_attention.jl:35);
+//  * Float32 arithmetic uses explicitly rounded intrinsics (__fmul_rn,
+//    __fadd_rn, __fdiv_rn, __fsqrt_rn) in the reference CPU operation order
+//    (src/backbone_cpu.jl), so no multiply-add is contracted;
+//  * no kernel traps: bad ids set a flag and poison their row with NaN.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qdc {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kThreads = 256;  // 8 warps per CTA for the vector kernels
+
+// ---------------------------------------------------------------- memory ops
+
+__device__ __forceinline__ float4 ld_nc_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint4 ld_nc_u4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_f4(float* p, float4 v) {
+    asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x),
+                 "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_u4(void* p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
+                 "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_u2(void* p, uint2 v) {
+    asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y)
+                 : "memory");
+}
+
+// ------------------------------------------------------------ bf16 storage
+// src/safetensors.jl:28-30 (decode: bits << 16) and :38-42 (encode: round to
+// nearest even by integer add, no NaN special case).
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t bf16_bits(float f) {
+    uint32_t b = __float_as_uint(f);
+    return (b + 0x00007fffu + ((b >> 16) & 1u)) >> 16;
+}
+
+__device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
+    return bf16_bits(lo) | (bf16_bits(hi) << 16);
+}
+
+// A 16-byte chunk of a row: 4 Float32 or 8 bf16 values, held as Float32.
+template <typename T> struct Chunk;
+
+template <> struct Chunk<float> {
+    static constexpr int N = 4;
+    float v[4];
+    __device__ __forceinline__ void load(const float* p) {
+        float4 t = ld_nc_f4(p);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    }
+    __device__ __forceinline__ void store(float* p) const {
+        st_f4(p, make_float4(v[0], v[1], v[2], v[3]));
+    }
+};
+
+template <> struct Chunk<uint16_t> {
+    static constexpr int N = 8;
+    float v[8];
+    __device__ __forceinline__ void load(const uint16_t* p) {
+        uint4 t = ld_nc_u4(p);
+        v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x);
+        v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
+        v[4] = bf16_lo(t.z); v[5] = bf16_hi(t.z);
+        v[6] = bf16_lo(t.w); v[7] = bf16_hi(t.w);
+    }
+    __device__ __forceinline__ void store(uint16_t* p) const {
+        st_u4(p, make_uint4(bf16_pack(v[0], v[1]), bf16_pack(v[2], v[3]),
+                            bf16_pack(v[4], v[5]), bf16_pack(v[6], v[7])));
+    }
+};
+
+template <typename T> __device__ __forceinline__ float scalar_load(const T* p);
+template <> __device__ __forceinline__ float scalar_load<float>(const float* p) { return __ldg(p); }
+template <> __device__ __forceinline__ float scalar_load<uint16_t>(const uint16_t* p) {
+    return __uint_as_float(uint32_t(__ldg(p)) << 16);
+}
+template <typename T> __device__ __forceinline__ void scalar_store(T* p, float v);
+template <> __device__ __forceinline__ void scalar_store<float>(float* p, float v) { *p = v; }
+template <> __device__ __forceinline__ void scalar_store<uint16_t>(uint16_t* p, float v) {
+    *p = uint16_t(bf16_bits(v));
+}
+
+// ------------------------------------------------------------------- math
+
+// Sum over a segment of `width` lanes (a power of two <= 32) of the warp.
+template <int WIDTH>
+__device__ __forceinline__ float segment_sum(float s) {
+#pragma unroll
+    for (int off = WIDTH / 2; off > 0; off >>= 1) s += __shfl_xor_sync(kFull, s, off);
+    return s;
+}
+
+// scale = inv(sqrt(sum / width + eps)), src/backbone_cpu.jl:344, each step
+// rounded once.
+__device__ __forceinline__ float rms_scale(float sumsq, float width, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, width), eps)));
+}
+
+// silu(x) = x * inv(1 + exp(-x)), src/backbone.jl:196-197 (accurate expf).
+__device__ __forceinline__ float silu(float x) {
+    return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
+}
+
+// ------------------------------------------------------------ row kernels
+// r = x (+ m), y = rms(r) * gamma_term; x optionally gathered by id.
+
+struct RowArgs {
+    void* out_r;
+    void* out_y;
+    const void* x;
+    const void* m;
+    const float* gamma;
+    const int32_t* ids;  // device ids: x row = x + ids[row] * ld_x
+    int* flag;           // raised on an out-of-range id
+    float eps;
+    int centered;
+    int64_t rows, width, ld_x, ld_m, ld_r, ld_y, vocab;
+};
+
+template <typename T>
+__device__ __forceinline__ const T* row_source(const RowArgs& a, int64_t row, bool& bad) {
+    if (a.ids) {
+        int32_t id = __ldg(a.ids + row);
+        bad = id < 0 || int64_t(id) >= a.vocab;
+        return static_cast<const T*>(a.x) + (bad ? int64_t(0) : int64_t(id)) * a.ld_x;
+    }
+    bad = false;
+    return static_cast<const T*>(a.x) + row * a.ld_x;
+}
+
+// Width = 32 lanes x CHUNKS x (16 bytes / sizeof(T)); every operand 16-byte
+// aligned with 16-byte-multiple leading dimensions (checked on the host).
+template <typename T, int CHUNKS>
+__global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
+    using C = Chunk<T>;
+    constexpr int N = C::N;
+    constexpr int W = 32 * N * CHUNKS;
+    __shared__ __align__(16) float gterm[W];
+    if (a.gamma) {  // gamma is NULL for a plain gather (no y output)
+        for (int i = threadIdx.x; i < W; i += blockDim.x)
+            gterm[i] = a.centered ? __fadd_rn(1.0f, a.gamma[i]) : a.gamma[i];
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t stride = int64_t(gridDim.x) * warps;
+    for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < a.rows;
+         row += stride) {
+        bool bad;
+        const T* xr = row_source<T>(a, row, bad);
+        C v[CHUNKS];
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) v[c].load(xr + (c * 32 + lane) * N);
+        if (a.m) {
+            const T* mr = static_cast<const T*>(a.m) + row * a.ld_m;
+            C w[CHUNKS];
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c) w[c].load(mr + (c * 32 + lane) * N);
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+                for (int j = 0; j < N; ++j) v[c].v[j] = __fadd_rn(v[c].v[j], w[c].v[j]);
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+            for (int j = 0; j < N; ++j) s = __fmaf_rn(v[c].v[j], v[c].v[j], s);
+        s = segment_sum<32>(s);
+        const float scale = rms_scale(s, float(W), a.eps);
+        if (bad) {
+            if (lane == 0) atomicOr(a.flag, 1);
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+                for (int j = 0; j < N; ++j) v[c].v[j] = __int_as_float(0x7fc00000);
+        }
+        if (a.out_r) {
+            T* rr = static_cast<T*>(a.out_r) + row * a.ld_r;
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c) v[c].store(rr + (c * 32 + lane) * N);
+        }
+        if (a.out_y) {
+            T* yr = static_cast<T*>(a.out_y) + row * a.ld_y;
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c) {
+                const float* g = gterm + (c * 32 + lane) * N;
+#pragma unroll
+                for (int j = 0; j < N; ++j)
+                    v[c].v[j] = bad ? v[c].v[j] : __fmul_rn(__fmul_rn(v[c].v[j], scale), g[j]);
+                v[c].store(yr + (c * 32 + lane) * N);
+            }
+        }
+    }
+}
+
+// Any width / alignment: warp per row, scalar loads, two passes (the second
+// pass re-reads x and m, which are still in L1/L2).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t stride = int64_t(gridDim.x) * warps;
+    const float width = float(a.width);
+    for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < a.rows;
+         row += stride) {
+        bool bad;
+        const T* xr = row_source<T>(a, row, bad);
+        const T* mr = a.m ? static_cast<const T*>(a.m) + row * a.ld_m : nullptr;
+        float s = 0.0f;
+        for (int64_t i = lane; i < a.width; i += 32) {
+            float r = scalar_load(xr + i);
+            if (mr) r = __fadd_rn(r, scalar_load(mr + i));
+            s = __fmaf_rn(r, r, s);
+        }
+        s = segment_sum<32>(s);
+        const float scale = rms_scale(s, width, a.eps);
+        if (bad && lane == 0) atomicOr(a.flag, 1);
+        T* rr = a.out_r ? static_cast<T*>(a.out_r) + row * a.ld_r : nullptr;
+        T* yr = a.out_y ? static_cast<T*>(a.out_y) + row * a.ld_y : nullptr;
+        for (int64_t i = lane; i < a.width; i += 32) {
+            float r = scalar_load(xr + i);
+            if (mr) r = __fadd_rn(r, scalar_load(mr + i));
+            if (bad) r = __int_as_float(0x7fc00000);
+            if (rr) scalar_store(rr + i, r);
+            if (yr) {
+                const float g = a.centered ? __fadd_rn(1.0f, a.gamma[i]) : a.gamma[i];
+                scalar_store(yr + i, bad ? r : __fmul_rn(__fmul_rn(r, scale), g));
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------- head kernels
+// A "unit" is one (token, head) vector of `dim` Float32 values.  LPU lanes
+// share a unit (LPU = min(32, dim/4)); 32/LPU units per warp; U units per
+// segment per iteration (their loads are all issued first).
+
+struct HeadArgs {
+    float* out;
+    const float* in;     // qk: input projection; gated: o
+    const float* z;      // gated only
+    const float* gamma;
+    const float* cos_tab;
+    const float* sin_tab;
+    float eps;
+    int heads, dim, rotary;
+    int64_t units;       // tokens * heads
+    int64_t in_tok, in_head;
+    int64_t z_tok, z_off;
+    int64_t out_tok;
+    int64_t pos_offset, seq_len;
+};
+
+template <int LPU, int CHUNKS, int U, bool GATED>
+__global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
+    constexpr int D = 4 * LPU * CHUNKS;
+    constexpr int UPW = 32 / LPU;
+    __shared__ __align__(16) float gterm[D];
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        gterm[i] = GATED ? a.gamma[i] : __fadd_rn(1.0f, a.gamma[i]);
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int seg = lane / LPU;
+    const int l = lane % LPU;
+    const int warps = blockDim.x >> 5;
+    const int64_t per_iter = int64_t(UPW) * U;
+    const int64_t stride = int64_t(gridDim.x) * warps * per_iter;
+    const int half = a.rotary >> 1;
+    const int hl = half >> 2;  // lanes per rotary half
+
+    for (int64_t base = (int64_t(blockIdx.x) * warps + (threadIdx.x >> 5)) * per_iter;
+         base < a.units; base += stride) {
+        float4 v[U][CHUNKS];
+        float4 zz[GATED ? U : 1][GATED ? CHUNKS : 1];
+        int64_t tok[U];
+        int hd[U];
+        bool live[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int64_t u = base + int64_t(k) * UPW + seg;
+            live[k] = u < a.units;
+            tok[k] = live[k] ? u / a.heads : 0;
+            hd[k] = live[k] ? int(u - tok[k] * a.heads) : 0;
+            const float* src = a.in + tok[k] * a.in_tok + int64_t(hd[k]) * a.in_head;
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c)
+                v[k][c] = live[k] ? ld_nc_f4(src + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);
+            if constexpr (GATED) {
+                const float* zs = a.z + tok[k] * a.z_tok + a.z_off + int64_t(hd[k]) * D;
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c)
+                    zz[k][c] = live[k] ? ld_nc_f4(zs + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            float s = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c) {
+                s = __fmaf_rn(v[k][c].x, v[k][c].x, s);
+                s = __fmaf_rn(v[k][c].y, v[k][c].y, s);
+                s = __fmaf_rn(v[k][c].z, v[k][c].z, s);
+                s = __fmaf_rn(v[k][c].w, v[k][c].w, s);
+            }
+            s = segment_sum<LPU>(s);
+            const float scale = rms_scale(s, float(D), a.eps);
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c) {
+                const float4 g = *reinterpret_cast<const float4*>(gterm + (c * LPU + l) * 4);
+                float4& x = v[k][c];
+                x.x = __fmul_rn(__fmul_rn(x.x, scale), g.x);
+                x.y = __fmul_rn(__fmul_rn(x.y, scale), g.y);
+                x.z = __fmul_rn(__fmul_rn(x.z, scale), g.z);
+                x.w = __fmul_rn(__fmul_rn(x.w, scale), g.w);
+                if constexpr (GATED) {
+                    x.x = __fmul_rn(x.x, silu(zz[k][c].x));
+                    x.y = __fmul_rn(x.y, silu(zz[k][c].y));
+                    x.z = __fmul_rn(x.z, silu(zz[k][c].z));
+                    x.w = __fmul_rn(x.w, silu(zz[k][c].w));
+                }
+            }
+            if constexpr (!GATED) {
+                // Rotate-half RoPE on dims [0, rotary) of chunk 0,
+                // src/backbone_cpu.jl:125-136: lanes [0, hl) hold a, lanes
+                // [hl, 2hl) hold b; the partner half arrives by shuffle.
+                if (hl > 0) {
+                    const int partner = seg * LPU + (l < hl ? l + hl : (l < 2 * hl ? l - hl : l));
+                    float4 p;
+                    p.x = __shfl_sync(kFull, v[k][0].x, partner);
+                    p.y = __shfl_sync(kFull, v[k][0].y, partner);
+                    p.z = __shfl_sync(kFull, v[k][0].z, partner);
+                    p.w = __shfl_sync(kFull, v[k][0].w, partner);
+                    if (live[k] && l < 2 * hl) {
+                        const int64_t pos =
+                            a.pos_offset + (a.seq_len > 0 ? tok[k] % a.seq_len : tok[k]);
+                        const int j = (l < hl ? l : l - hl) * 4;
+                        const float4 cs = ld_nc_f4(a.cos_tab + pos * half + j);
+                        const float4 sn = ld_nc_f4(a.sin_tab + pos * half + j);
+                        float4& x = v[k][0];
+                        if (l < hl) {  // a*cos - b*sin
+                            x.x = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(p.x, sn.x));
+                            x.y = __fsub_rn(__fmul_rn(x.y, cs.y), __fmul_rn(p.y, sn.y));
+                            x.z = __fsub_rn(__fmul_rn(x.z, cs.z), __fmul_rn(p.z, sn.z));
+                            x.w = __fsub_rn(__fmul_rn(x.w, cs.w), __fmul_rn(p.w, sn.w));
+                        } else {       // b*cos + a*sin
+                            x.x = __fadd_rn(__fmul_rn(x.x, cs.x), __fmul_rn(p.x, sn.x));
+                            x.y = __fadd_rn(__fmul_rn(x.y, cs.y), __fmul_rn(p.y, sn.y));
+                            x.z = __fadd_rn(__fmul_rn(x.z, cs.z), __fmul_rn(p.z, sn.z));
+                            x.w = __fadd_rn(__fmul_rn(x.w, cs.w), __fmul_rn(p.w, sn.w));
+                        }
+                    }
+                }
+            }
+            if (live[k]) {
+                float* dst = a.out + tok[k] * a.out_tok + int64_t(hd[k]) * D;
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c) st_f4(dst + (c * LPU + l) * 4, v[k][c]);
+            }
+        }
+    }
+}
+
+// Any dim / rotary / alignment: warp per unit, scalar loads; the RoPE
+// partner is recomputed from its own input element.
+template <bool GATED>
+__global__ void __launch_bounds__(kThreads) head_norm_generic(HeadArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t stride = int64_t(gridDim.x) * warps;
+    const int half = a.rotary >> 1;
+    for (int64_t u = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); u < a.units; u += stride) {
+        const int64_t tok = u / a.heads;
+        const int hd = int(u - tok * a.heads);
+        const float* src = a.in + tok * a.in_tok + int64_t(hd) * a.in_head;
+        float s = 0.0f;
+        for (int i = lane; i < a.dim; i += 32) {
+            const float x = __ldg(src + i);
+            s = __fmaf_rn(x, x, s);
+        }
+        s = segment_sum<32>(s);
+        const float scale = rms_scale(s, float(a.dim), a.eps);
+        float* dst = a.out + tok * a.out_tok + int64_t(hd) * a.dim;
+        if constexpr (GATED) {
+            const float* zs = a.z + tok * a.z_tok + a.z_off + int64_t(hd) * a.dim;
+            for (int i = lane; i < a.dim; i += 32) {
+                const float y = __fmul_rn(__fmul_rn(__ldg(src + i), scale), a.gamma[i]);
+                dst[i] = __fmul_rn(y, silu(__ldg(zs + i)));
+            }
+        } else {
+            const int64_t pos = a.pos_offset + (a.seq_len > 0 ? tok % a.seq_len : tok);
+            for (int i = lane; i < a.dim; i += 32) {
+                const float y = __fmul_rn(__fmul_rn(__ldg(src + i), scale),
+                                          __fadd_rn(1.0f, a.gamma[i]));
+                float out = y;
+                if (i < 2 * half) {
+                    const int j = i < half ? i : i - half;
+                    const int q = i < half ? i + half : i - half;
+                    const float p = __fmul_rn(__fmul_rn(__ldg(src + q), scale),
+                                              __fadd_rn(1.0f, a.gamma[q]));
+                    const float c = __ldg(a.cos_tab + pos * half + j);
+                    const float sn = __ldg(a.sin_tab + pos * half + j);
+                    out = i < half ? __fsub_rn(__fmul_rn(y, c), __fmul_rn(p, sn))
+                                   : __fadd_rn(__fmul_rn(y, c), __fmul_rn(p, sn));
+                }
+                dst[i] = out;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- SwiGLU
+
+struct SwigluArgs {
+    float* out_f32;
+    uint16_t* out_bf16;
+    const float* g;
+    const float* u;
+    int64_t rows, width, ld_g, ld_u, ld_out;
+};
+
+// Warp per row, 4 x 16-byte loads of g and of u in flight per lane.
+template <bool F32, bool BF16>
+__global__ void __launch_bounds__(kThreads) swiglu_vec(SwigluArgs a) {
+    constexpr int U = 4;
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t stride = int64_t(gridDim.x) * warps;
+    const int wv = int(a.width >> 2);
+    for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < a.rows;
+         row += stride) {
+        const float* gr = a.g + row * a.ld_g;
+        const float* ur = a.u + row * a.ld_u;
+        for (int c0 = lane; c0 < wv; c0 += 32 * U) {
+            float4 gv[U], uv[U];
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const int c = c0 + 32 * k;
+                if (c < wv) {
+                    gv[k] = ld_nc_f4(gr + 4 * c);
+                    uv[k] = ld_nc_f4(ur + 4 * c);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const int c = c0 + 32 * k;
+                if (c < wv) {
+                    float4 h;
+                    h.x = __fmul_rn(silu(gv[k].x), uv[k].x);
+                    h.y = __fmul_rn(silu(gv[k].y), uv[k].y);
+                    h.z = __fmul_rn(silu(gv[k].z), uv[k].z);
+                    h.w = __fmul_rn(silu(gv[k].w), uv[k].w);
+                    if (F32) st_f4(a.out_f32 + row * a.ld_out + 4 * c, h);
+                    if (BF16)
+                        st_u2(a.out_bf16 + row * a.ld_out + 4 * c,
+                              make_uint2(bf16_pack(h.x, h.y), bf16_pack(h.z, h.w)));
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) swiglu_generic(SwigluArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t stride = int64_t(gridDim.x) * warps;
+    for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < a.rows;
+         row += stride) {
+        for (int64_t i = lane; i < a.width; i += 32) {
+            const float h = __fmul_rn(silu(__ldg(a.g + row * a.ld_g + i)),
+                                      __ldg(a.u + row * a.ld_u + i));
+            if (a.out_f32) a.out_f32[row * a.ld_out + i] = h;
+            if (a.out_bf16) a.out_bf16[row * a.ld_out + i] = uint16_t(bf16_bits(h));
+        }
+    }
+}
+
+}  // namespace qdc

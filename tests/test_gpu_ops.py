@@ -1,0 +1,318 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the CPU oracle.
+
+Bar: the gather bit-exact; Float32 outputs within |a - b| <= 1e-6 + 1e-5 |b|;
+bf16-stored outputs within 1e-2 relative.  Cases follow the reference's op
+tests (odd widths 1/7, rows 0/1/17, rotary 0/2/4, packed projection
+layouts, NaN-filled outputs that must be overwritten, inputs unchanged) plus
+the BASELINE shapes (hidden 1024, head_dim 256 / rotary 64, Dv 128,
+intermediate 3584).
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-6, 1e-5
+BF16_RTOL = 1e-2
+
+
+def f32_close(actual, expected):
+    a = actual.detach().cpu().numpy().astype(np.float64) if torch.is_tensor(actual) else actual
+    e = np.asarray(expected, np.float64)
+    ok = np.abs(a - e) <= ATOL + RTOL * np.abs(e)
+    ok |= np.isnan(a) & np.isnan(e)
+    return bool(ok.all())
+
+
+def bf16_close(actual_bf16, expected_bits, oracle):
+    a = actual_bf16.detach().cpu().view(torch.int16).numpy().view(np.uint16)
+    av = oracle.bf16_decode(a).astype(np.float64)
+    ev = oracle.bf16_decode(expected_bits).astype(np.float64)
+    return bool((np.abs(av - ev) <= 1e-6 + BF16_RTOL * np.abs(ev)).all())
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def dev_bf16(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).cuda().view(torch.bfloat16)
+
+
+def nan_like(shape, dtype=torch.float32):
+    return torch.full(shape, float("nan"), dtype=dtype, device="cuda")
+
+
+@pytest.fixture(scope="module")
+def q():
+    import qdc_b200
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return qdc_b200
+
+
+def rng(seed=0):
+    return np.random.default_rng(seed)
+
+
+# --------------------------------------------------------------- gather
+
+@pytest.mark.parametrize("hidden", [1024, 256, 8, 1000])
+@pytest.mark.parametrize("n", [0, 1, 17, 513])
+def test_gather_bit_exact(q, oracle, hidden, n):
+    r = rng(hidden + n)
+    table = r.normal(0, 0.02, (4096, hidden)).astype(np.float32)
+    ids = r.integers(0, 4096, n).astype(np.int32)
+    out = q.native_gather(dev(table), ids)
+    assert out.shape == (n, hidden)
+    assert np.array_equal(out.cpu().numpy(), oracle.gather(table, ids))
+    # bf16 table: bit-exact copy of the stored bits
+    t16 = oracle.bf16_encode(table)
+    out16 = q.native_gather(dev_bf16(t16), ids)
+    assert np.array_equal(out16.cpu().view(torch.int16).numpy().view(np.uint16), t16[ids])
+
+
+def test_gather_rejects_out_of_vocab_before_launch(q):
+    table = dev(np.zeros((64, 8), np.float32))
+    with pytest.raises(q.ArgumentError):
+        q.native_gather(table, [1, 64])
+    with pytest.raises(q.ArgumentError):
+        q.native_gather(table, [-1])
+
+
+def test_gather_device_ids_flag(q, oracle):
+    table = rng(1).normal(0, 1, (64, 256)).astype(np.float32)
+    ids = np.array([5, 64, 7, -3], np.int32)
+    ctx = q.context(0)
+    out = q.native_gather(dev(table), dev(ids), ctx=ctx)
+    with pytest.raises(q.ArgumentError):
+        ctx.sync()
+    o = out.cpu().numpy()
+    assert np.array_equal(o[0], table[5]) and np.array_equal(o[2], table[7])
+    assert np.isnan(o[1]).all() and np.isnan(o[3]).all()
+    ctx.sync()  # flag cleared by the previous report
+
+
+@pytest.mark.parametrize("hidden", [1024, 256, 7])
+@pytest.mark.parametrize("with_add", [False, True])
+@pytest.mark.parametrize("centered", [True, False])
+def test_gather_rms_f32(q, oracle, hidden, with_add, centered):
+    r = rng(hidden)
+    n, vocab = 77, 5000
+    table = r.normal(0, 0.02, (vocab, hidden)).astype(np.float32)
+    ids = r.integers(0, vocab, n).astype(np.int32)
+    add = r.normal(0, 1, (n, hidden)).astype(np.float32) if with_add else None
+    w = r.normal(0, 0.02, hidden).astype(np.float32)
+    ex_r, ex_y = oracle.gather_rms(table, ids, add, w, 1e-6, centered)
+    out_x, out_y = nan_like((n, hidden)), nan_like((n, hidden))
+    x, y = q.native_gather_rms(dev(table), ids, dev(w), 1e-6, add=None if add is None else dev(add),
+                               centered=centered, out_x=out_x, out_y=out_y)
+    assert np.array_equal(x.cpu().numpy(), ex_r)  # r = E[id] + add: one Float32 add, exact
+    assert f32_close(y, ex_y)
+
+
+@pytest.mark.parametrize("hidden", [1024, 512, 24])
+def test_gather_rms_bf16(q, oracle, hidden):
+    r = rng(7)
+    n, vocab = 300, 3000
+    table = oracle.bf16_encode(r.normal(0, 0.02, (vocab, hidden)).astype(np.float32))
+    add = oracle.bf16_encode(r.normal(0, 1, (n, hidden)).astype(np.float32))
+    ids = r.integers(0, vocab, n).astype(np.int32)
+    w = r.normal(0, 0.02, hidden).astype(np.float32)
+    ex_r, ex_y = oracle.gather_rms(table, ids, add, w, 1e-6)
+    x, y = q.native_gather_rms(dev_bf16(table), ids, dev(w), 1e-6, add=dev_bf16(add))
+    assert bf16_close(x, ex_r, oracle) and bf16_close(y, ex_y, oracle)
+
+
+# ---------------------------------------------------------- residual RMS
+
+@pytest.mark.parametrize("width", [1, 7, 128, 256, 768, 1024, 2048, 1000, 4096])
+@pytest.mark.parametrize("rows", [0, 1, 17, 300])
+def test_residual_rms_f32(q, oracle, width, rows):
+    r = rng(width * 1000 + rows)
+    x = r.normal(0, 1, (rows, width)).astype(np.float32)
+    m = r.normal(0, 1, (rows, width)).astype(np.float32)
+    w = r.normal(0, 0.02, width).astype(np.float32)
+    ex_r, ex_y = oracle.residual_rms(x, m, w, 1e-6)
+    dx, dm = dev(x), dev(m)
+    out_r, out_y = nan_like((rows, width)), nan_like((rows, width))
+    res, y = q.native_residual_rms(dx, dm, dev(w), 1e-6, out_r=out_r, out_y=out_y)
+    assert np.array_equal(res.cpu().numpy(), ex_r)
+    assert f32_close(y, ex_y)
+    assert np.array_equal(dx.cpu().numpy(), x) and np.array_equal(dm.cpu().numpy(), m)
+    # plain RMSNorm (input / final norm), centered and not
+    for centered in (True, False):
+        y2 = q.native_rms(dx, dev(w), 1e-6, centered=centered)
+        assert f32_close(y2, oracle.rms(x, w, 1e-6, centered=centered))
+
+
+def test_residual_rms_in_place_and_strided(q, oracle):
+    r = rng(3)
+    rows, width, ld = 65, 1024, 1536
+    big = r.normal(0, 1, (rows, ld)).astype(np.float32)
+    m = r.normal(0, 1, (rows, width)).astype(np.float32)
+    w = r.normal(0, 0.02, width).astype(np.float32)
+    ex_r, ex_y = oracle.residual_rms(big[:, :width], m, w, 1e-6)
+    dbig = dev(big)
+    view = dbig[:, :width]
+    res, y = q.native_residual_add_rms(view, dev(m), dev(w), 1e-6)
+    assert res.data_ptr() == view.data_ptr()
+    got = dbig.cpu().numpy()
+    assert np.array_equal(got[:, :width], ex_r)
+    assert np.array_equal(got[:, width:], big[:, width:])  # padding untouched
+    assert f32_close(y, ex_y)
+
+
+@pytest.mark.parametrize("width", [1024, 256, 40])
+def test_residual_rms_bf16(q, oracle, width):
+    r = rng(width)
+    rows = 129
+    x = oracle.bf16_encode(r.normal(0, 1, (rows, width)).astype(np.float32))
+    m = oracle.bf16_encode(r.normal(0, 1, (rows, width)).astype(np.float32))
+    w = r.normal(0, 0.02, width).astype(np.float32)
+    ex_r, ex_y = oracle.residual_rms_bf16(x, m, w, 1e-6)
+    res, y = q.native_residual_rms(dev_bf16(x), dev_bf16(m), dev(w), 1e-6)
+    assert bf16_close(res, ex_r, oracle) and bf16_close(y, ex_y, oracle)
+
+
+def test_rms_edge_values(q, oracle):
+    x = np.zeros((4, 1024), np.float32)
+    x[1] = 1e-30
+    x[2, :3] = np.float32(3e38)  # overflowing sum of squares -> scale 0
+    x[3] = np.nan
+    w = np.zeros(1024, np.float32)
+    y = q.native_rms(dev(x), dev(w), 1e-6)
+    assert f32_close(y, oracle.rms(x, w, 1e-6))
+
+
+def test_residual_rms_validation(q):
+    x = torch.zeros(4, 8, device="cuda")
+    with pytest.raises(q.DimensionMismatch):
+        q.native_residual_rms(x, torch.zeros(4, 9, device="cuda"), torch.zeros(8, device="cuda"), 1e-6)
+    with pytest.raises(q.DimensionMismatch):
+        q.native_rms(x, torch.zeros(7, device="cuda"), 1e-6)
+
+
+# ----------------------------------------------------------- q/k norm + RoPE
+
+QK_CASES = [  # tokens, heads, dim, rotary, packed (q inside a [q;gate] projection)
+    (17, 8, 256, 64, True), (33, 2, 256, 64, False), (40, 4, 64, 16, True), (9, 2, 4, 4, True),
+    (9, 2, 4, 2, False), (9, 1, 4, 0, False), (13, 3, 128, 128, False), (7, 2, 96, 32, True),
+    (5, 2, 256, 256, False), (1, 8, 256, 64, True), (0, 8, 256, 64, True), (21, 2, 512, 64, False),
+    (11, 2, 32, 8, False),
+]
+
+
+@pytest.mark.parametrize("tokens,heads,dim,rotary,packed", QK_CASES)
+def test_qk_norm_rope(q, oracle, tokens, heads, dim, rotary, packed):
+    r = rng(tokens * 31 + dim + rotary)
+    width = 2 * dim if packed else dim
+    proj = r.normal(0, 1, (tokens, heads, width)).astype(np.float32)
+    w = r.normal(0, 0.02, dim).astype(np.float32)
+    cos, sin = oracle.rope_table(1e7, rotary, max(tokens, 1))
+    expected = oracle.qk_norm_rope(proj[:, :, :dim], w, 1e-6, rotary, cos, sin)
+    dproj = dev(proj)
+    out = nan_like((tokens, heads, dim))
+    dc, ds = q.rope_table(1e7, rotary, max(tokens, 1), device="cuda")
+    got = q.native_qk_norm_rope(dproj[:, :, :dim], dev(w), 1e-6, rotary, dc, ds, out=out)
+    assert f32_close(got, expected)
+    assert np.array_equal(dproj.cpu().numpy(), proj)
+
+
+def test_qk_positions_sequence_sharded(q, oracle):
+    """pos = offset + t mod seq_len: sequences packed back to back (the
+    multi-GPU shard layout) and the final-query offset of
+    src/backbone_cpu.jl:1012-1016."""
+    r = rng(11)
+    seqs, seq_len, heads, dim, rotary = 3, 50, 2, 256, 64
+    x = r.normal(0, 1, (seqs * seq_len, heads, dim)).astype(np.float32)
+    w = r.normal(0, 0.02, dim).astype(np.float32)
+    cos, sin = oracle.rope_table(1e7, rotary, 2048)
+    dc, ds = q.rope_table(1e7, rotary, 2048, device="cuda")
+    got = q.native_qk_norm_rope(dev(x), dev(w), 1e-6, rotary, dc, ds, seq_len=seq_len)
+    for s in range(seqs):
+        sl = slice(s * seq_len, (s + 1) * seq_len)
+        assert f32_close(got[sl], oracle.qk_norm_rope(x[sl], w, 1e-6, rotary, cos, sin))
+    last = q.native_qk_norm_rope(dev(x[-1:]), dev(w), 1e-6, rotary, dc, ds, pos_offset=2047)
+    assert f32_close(last, oracle.qk_norm_rope(x[-1:], w, 1e-6, rotary, cos, sin, pos_offset=2047))
+    with pytest.raises(q.ArgumentError):  # beyond the table
+        q.native_qk_norm_rope(dev(x[-2:]), dev(w), 1e-6, rotary, dc, ds, pos_offset=2047)
+
+
+# --------------------------------------------------------------- gated RMS
+
+GATED_CASES = [(17, 16, 128), (5, 4, 128), (9, 2, 2), (33, 3, 64), (1, 16, 128), (0, 16, 128),
+               (12, 2, 256), (7, 5, 48)]
+
+
+@pytest.mark.parametrize("rows,heads,dim", GATED_CASES)
+def test_gated_rms(q, oracle, rows, heads, dim):
+    r = rng(rows + heads + dim)
+    o = r.normal(0, 1, (rows, heads, dim)).astype(np.float32)
+    # z lives inside a packed [qkv | z | a | b] projection row
+    lead, tail = 3 * dim * heads + (4 if dim % 4 == 0 else 1), 8
+    packed = r.normal(0, 1, (rows, lead + heads * dim + tail)).astype(np.float32)
+    z = packed[:, lead:lead + heads * dim].reshape(rows, heads, dim)
+    w = (1 + r.normal(0, 0.02, dim)).astype(np.float32)
+    expected = oracle.gated_rms(o, np.ascontiguousarray(z), w, 1e-6)
+    dpacked = dev(packed)
+    dz = dpacked[:, lead:lead + heads * dim].view(rows, heads, dim) if rows else \
+        torch.empty((0, heads, dim), device="cuda")
+    got = q.native_gated_rms(dev(o), dz, dev(w), 1e-6, out=nan_like((rows, heads * dim)))
+    assert f32_close(got, expected)
+
+
+# ------------------------------------------------------------------ SwiGLU
+
+@pytest.mark.parametrize("rows,width", [(17, 3584), (3, 768), (5, 16), (7, 13), (1, 4), (0, 64),
+                                        (33, 1000)])
+@pytest.mark.parametrize("packed", [True, False])
+def test_swiglu(q, oracle, rows, width, packed):
+    r = rng(rows * width)
+    if packed:  # [gate | up] per token, ext/cuda_mlp.jl:63-71
+        proj = r.normal(0, 1, (rows, 2 * width)).astype(np.float32)
+        g, u = proj[:, :width], proj[:, width:]
+        dproj = dev(proj)
+        dg, du = dproj[:, :width], dproj[:, width:]
+    else:
+        g = r.normal(0, 1, (rows, width)).astype(np.float32)
+        u = r.normal(0, 1, (rows, width)).astype(np.float32)
+        dg, du = dev(g), dev(u)
+    e32, e16 = oracle.swiglu(np.ascontiguousarray(g), np.ascontiguousarray(u), want_bf16=True)
+    h32, h16 = q.native_mlp_gate(dg, du, want_bf16=True, out_f32=nan_like((rows, width)))
+    assert f32_close(h32, e32) and bf16_close(h16, e16, oracle)
+    only16 = q.native_mlp_gate(dg, du, want_f32=False, want_bf16=True)[1]
+    assert bf16_close(only16, e16, oracle)
+
+
+def test_swiglu_edges(q, oracle):
+    g = np.array([[0.0, -0.0, 1.0, -1.0, 30.0, -30.0, 100.0, -100.0, 88.0, -88.0, 1e-30, -1e-30]],
+                 np.float32)
+    u = np.full_like(g, 3.0)
+    e32, _ = oracle.swiglu(g, u)
+    h32, _ = q.native_mlp_gate(dev(g), dev(u))
+    assert f32_close(h32, e32)
+    assert np.array_equal(np.signbit(h32.cpu().numpy()), np.signbit(e32))
+
+
+# ---------------------------------------------------------------- workspace
+
+def test_workspace_arena(q):
+    ctx = q.Context(0)
+    ctx.ws_reserve(1 << 20)
+    used, cap, _ = ctx.ws_stats()
+    assert used == 0 and cap >= 1 << 20
+    a = ctx.ws_tensor((100, 3))
+    mark = ctx.ws_mark()
+    b = ctx.ws_tensor((10,), torch.bfloat16)
+    assert b.data_ptr() % 256 == 0 and b.data_ptr() >= a.data_ptr() + 1200
+    ctx.ws_release(mark)
+    c = ctx.ws_tensor((10,), torch.bfloat16)
+    assert c.data_ptr() == b.data_ptr()  # slot reused by call order
+    with pytest.raises(q.QdcError):
+        ctx.ws_alloc(cap)  # exhausted -> QDC_ENOMEM, nothing allocated
+    ctx.ws_reset()
+    assert ctx.ws_tensor((1,)).data_ptr() == a.data_ptr()
+    a.fill_(1.0)
+    torch.cuda.synchronize()
+    ctx.close()

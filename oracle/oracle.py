@@ -204,8 +204,10 @@ def rope_table(theta, rotary, n):
 def qk_norm_rope(x, weight, eps, rotary, cos, sin, pos_offset=0, seq_len=None):
     """x: (tokens, heads, dim) float32 view, unit inner stride (may be a
     slice of a packed projection).  Returns dense (tokens, heads, dim)."""
-    assert x.dtype == np.float32 and x.ndim == 3 and x.strides[2] == 4
     tokens, heads, dim = x.shape
+    if x.size == 0:
+        return np.empty((tokens, heads, dim), np.float32)
+    assert x.dtype == np.float32 and x.ndim == 3 and x.strides[2] == 4
     cos = _f32(cos)
     sin = _f32(sin)
     half = rotary // 2
@@ -232,6 +234,8 @@ def gated_rms(o, z, weight, eps):
     raw projection; silu is applied here.  Returns (rows, heads*dim)."""
     assert o.shape == z.shape and o.ndim == 3
     rows, heads, dim = o.shape
+    if o.size == 0:
+        return np.empty((rows, heads * dim), np.float32)
     for a in (o, z):
         assert a.dtype == np.float32 and a.strides[2] == 4
         assert heads <= 1 or a.strides[1] == 4 * dim
@@ -249,6 +253,9 @@ def swiglu(g, u, want_f32=True, want_bf16=False):
     """g, u: (rows, width) float32 views with unit inner stride."""
     assert g.shape == u.shape and g.dtype == np.float32 and u.dtype == np.float32
     rows, width = g.shape
+    if g.size == 0:
+        return (np.empty((rows, width), np.float32) if want_f32 else None,
+                np.empty((rows, width), np.uint16) if want_bf16 else None)
     out32 = np.empty((rows, width), np.float32) if want_f32 else None
     out16 = np.empty((rows, width), np.uint16) if want_bf16 else None
     lib().qdo_swiglu(_p(out32), _p(out16, _u16p), g.ctypes.data_as(_f32p),

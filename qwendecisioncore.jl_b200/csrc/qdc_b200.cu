@@ -182,6 +182,7 @@ int gather_checks(qdc_ctx* ctx, const void* out_x, const void* out_y, const void
     if (n < 0 || hidden < 1 || vocab < 1)
         return fail(ctx, QDC_EINVAL, "bad sizes n=%lld hidden=%lld vocab=%lld", (long long)n,
                     (long long)hidden, (long long)vocab);
+    if (n == 0) return QDC_OK;  // nothing to gather; empty outputs may be NULL
     if (table == nullptr) return fail(ctx, QDC_EINVAL, "table is NULL");
     if (gamma == nullptr && out_y != nullptr)
         return fail(ctx, QDC_EINVAL, "out_y given without gamma");
@@ -376,6 +377,7 @@ int qdc_residual_rms(qdc_ctx* ctx, void* out_r, void* out_y, const void* x, cons
                      int64_t ld_x, int64_t ld_m, int64_t ld_r, int64_t ld_y, int dtype, void* stream) {
     if (int s = check_ctx(ctx)) return s;
     if (rows < 0 || width < 1) return fail(ctx, QDC_EINVAL, "bad sizes rows=%lld width=%lld", (long long)rows, (long long)width);
+    if (rows == 0) return QDC_OK;
     if (x == nullptr || out_y == nullptr || gamma == nullptr)
         return fail(ctx, QDC_EINVAL, "x, out_y and gamma are required");
     if (ld_x < width || ld_y < width || (m && ld_m < width) || (out_r && ld_r < width))
@@ -494,6 +496,7 @@ int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, 
         return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d dim=%d", (long long)tokens, heads, dim);
     if (rotary < 0 || (rotary & 1) || rotary > dim)
         return fail(ctx, QDC_EINVAL, "rotary=%d must be even and <= dim=%d", rotary, dim);
+    if (tokens == 0) return QDC_OK;
     if (out == nullptr || in == nullptr || gamma == nullptr)
         return fail(ctx, QDC_EINVAL, "out, in and gamma are required");
     if (in_tok < 0 || in_head < 0) return fail(ctx, QDC_EINVAL, "negative stride");
@@ -519,6 +522,7 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
     if (int s = check_ctx(ctx)) return s;
     if (rows < 0 || heads < 1 || dim < 1)
         return fail(ctx, QDC_EINVAL, "bad sizes rows=%lld heads=%d dim=%d", (long long)rows, heads, dim);
+    if (rows == 0) return QDC_OK;
     if (out == nullptr || o == nullptr || z == nullptr || gamma == nullptr)
         return fail(ctx, QDC_EINVAL, "out, o, z and gamma are required");
     const int64_t row_width = int64_t(heads) * dim;
@@ -537,6 +541,7 @@ int qdc_swiglu(qdc_ctx* ctx, float* out_f32, uint16_t* out_bf16, const float* g,
                int64_t rows, int64_t width, int64_t ld_g, int64_t ld_u, int64_t ld_out, void* stream) {
     if (int s = check_ctx(ctx)) return s;
     if (rows < 0 || width < 1) return fail(ctx, QDC_EINVAL, "bad sizes rows=%lld width=%lld", (long long)rows, (long long)width);
+    if (rows == 0) return QDC_OK;
     if (g == nullptr || u == nullptr) return fail(ctx, QDC_EINVAL, "g and u are required");
     if (out_f32 == nullptr && out_bf16 == nullptr) return fail(ctx, QDC_EINVAL, "no output requested");
     if (ld_g < width || ld_u < width || ld_out < width)

@@ -166,6 +166,8 @@ def _rows(t, name):
     """(rows, width, ld) of a 2-D tensor with unit inner stride."""
     if t.dim() != 2:
         raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if t.numel() == 0:
+        return t.shape[0], t.shape[1], max(t.shape[1], 1)
     if t.shape[1] > 1 and t.stride(1) != 1:
         raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} needs a unit inner stride")
     ld = t.stride(0) if t.shape[0] > 1 else t.shape[1]

@@ -239,79 +239,142 @@ class LayerKernelStep:
 
 # ------------------------------------------------------ per-kernel configs
 
+def single_kernel(name, tokens, device, seed=1):
+    """One per-layer kernel on BASELINE-shaped inputs of `tokens` rows.
+    Returns (launch function, algorithmic bytes per launch)."""
+    import torch
+    import qdc_b200 as q
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    f = dict(dtype=torch.float32, device=device)
+    ctx = q.context(device)
+    T = tokens
+
+    def normal(shape, std=1.0):
+        return torch.randn(shape, generator=g, **f).mul_(std)
+
+    gam = normal((HIDDEN,), 0.02)
+    if name in ("gather_rms", "gather_rms_bf16"):
+        table = normal((VOCAB, HIDDEN), 0.02)
+        ids = torch.randint(0, VOCAB, (T,), generator=g, device=device, dtype=torch.int32)
+        resid = normal((T, HIDDEN))
+        if name.endswith("bf16"):
+            table, resid = table.to(torch.bfloat16), resid.to(torch.bfloat16)
+        ox, oy = torch.empty_like(resid), torch.empty_like(resid)
+        es = resid.element_size()
+        return (lambda: q.native_gather_rms(table, ids, gam, EPS, add=resid, out_x=ox, out_y=oy,
+                                            ctx=ctx),
+                4 * T * HIDDEN * es + T * 4 + HIDDEN * 4)
+    if name in ("post_rms", "post_rms_bf16"):
+        x, m = normal((T, HIDDEN)), normal((T, HIDDEN))
+        if name.endswith("bf16"):
+            x, m = x.to(torch.bfloat16), m.to(torch.bfloat16)
+        rr, yy = torch.empty_like(x), torch.empty_like(x)
+        return (lambda: q.native_residual_rms(x, m, gam, EPS, out_r=rr, out_y=yy, ctx=ctx),
+                4 * x.numel() * x.element_size() + HIDDEN * 4)
+    if name.startswith("swiglu"):
+        gu = normal((T, 2 * INTER))
+        gg, uu = gu[:, :INTER], gu[:, INTER:]
+        h32 = torch.empty((T, INTER), **f)
+        h16 = torch.empty((T, INTER), dtype=torch.bfloat16, device=device)
+        n = T * INTER
+        if name == "swiglu":
+            return lambda: q.native_mlp_gate(gg, uu, out_f32=h32, ctx=ctx), 12 * n
+        if name == "swiglu_bf16":
+            return lambda: q.native_mlp_gate(gg, uu, want_f32=False, out_bf16=h16, ctx=ctx), 10 * n
+        return lambda: q.native_mlp_gate(gg, uu, out_f32=h32, out_bf16=h16, ctx=ctx), 14 * n
+    if name == "gated_rms":
+        o = normal((T, HV, DV))
+        proj = normal((T, PROJ_W))
+        z = proj[:, Z_OFF:Z_OFF + HV * DV].view(T, HV, DV)
+        gv = normal((DV,), 0.02).add_(1.0)
+        out = torch.empty((T, HV * DV), **f)
+        return (lambda: q.native_gated_rms(o, z, gv, EPS, out=out, ctx=ctx),
+                3 * T * HV * DV * 4 + DV * 4)
+    if name in ("q_norm_rope", "k_norm_rope", "qk_norm_rope"):
+        cos, sin = q.rope_table(THETA, ROTARY, SEQ, device=device)
+        gq = normal((HEAD_DIM,), 0.02)
+        qgate = normal((T, HQ, 2 * HEAD_DIM))
+        kin = normal((T, HKV, HEAD_DIM))
+        qo = torch.empty((T, HQ, HEAD_DIM), **f)
+        ko = torch.empty_like(kin)
+        table = 2 * SEQ * (ROTARY // 2) * 4
+
+        def qn():
+            q.native_qk_norm_rope(qgate[:, :, :HEAD_DIM], gq, EPS, ROTARY, cos, sin, seq_len=SEQ,
+                                  out=qo, ctx=ctx)
+
+        def kn():
+            q.native_qk_norm_rope(kin, gq, EPS, ROTARY, cos, sin, seq_len=SEQ, out=ko, ctx=ctx)
+
+        if name == "q_norm_rope":
+            return qn, 2 * qo.numel() * 4 + table
+        if name == "k_norm_rope":
+            return kn, 2 * ko.numel() * 4 + table
+
+        def both():
+            qn()
+            kn()
+        return both, 2 * (qo.numel() + ko.numel()) * 4 + 2 * table
+    raise SystemExit(f"unknown kernel {name}")
+
+
+def time_launches(fn, device, reps, warmup=3):
+    """Average device time (us) of `reps` back-to-back launches."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize(device)
+    return s.elapsed_time(e) * 1e3 / reps
+
+
+CONFIG_CASES = [  # (report name, kernel, tokens): BASELINE configs 2-4
+    ("cfg2_gather_residual_rms_f32", "gather_rms", 16384),
+    ("cfg2_gather_residual_rms_bf16", "gather_rms_bf16", 16384),
+    ("cfg3_qk_norm_rope", "qk_norm_rope", 16384),
+    ("cfg4_post_residual_rms", "post_rms", 32768),
+    ("cfg4_swiglu_f32", "swiglu", 32768),
+    ("cfg4_swiglu_bf16", "swiglu_bf16", 32768),
+    ("cfg4_swiglu_f32_and_bf16", "swiglu_both", 32768),
+]
+
+
 def kernel_configs(device, peak, reps=20):
     """BASELINE configs 2-4 as single-kernel workloads: GB/s and fraction of
     the HBM peak, each averaged over `reps` back-to-back launches on inputs
     larger than L2."""
     import torch
-    import qdc_b200 as q
-    g = torch.Generator(device=device)
-    g.manual_seed(1)
-    f = dict(dtype=torch.float32, device=device)
     out = {}
-
-    def timed(fn, nbytes, name):
-        for _ in range(3):
-            fn()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(device)
-        s.record()
-        for _ in range(reps):
-            fn()
-        e.record()
-        torch.cuda.synchronize(device)
-        us = s.elapsed_time(e) * 1e3 / reps
+    for label, name, tokens in CONFIG_CASES:
+        fn, nbytes = single_kernel(name, tokens, device)
+        us = time_launches(fn, device, reps)
         gbs = nbytes / (us * 1e-6) / 1e9
-        out[name] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
-                     "bytes": nbytes}
-
-    ctx = q.context(device)
-    T = 16384
-    table = torch.randn((VOCAB, HIDDEN), generator=g, **f).mul_(0.02)
-    ids = torch.randint(0, VOCAB, (T,), generator=g, device=device, dtype=torch.int32)
-    resid = torch.randn((T, HIDDEN), generator=g, **f)
-    gam = torch.randn((HIDDEN,), generator=g, **f).mul_(0.02)
-    ox, oy = torch.empty((T, HIDDEN), **f), torch.empty((T, HIDDEN), **f)
-    nb = 4 * T * HIDDEN * 4 + T * 4 + HIDDEN * 4
-    timed(lambda: q.native_gather_rms(table, ids, gam, EPS, add=resid, out_x=ox, out_y=oy, ctx=ctx),
-          nb, "cfg2_gather_residual_rms_f32")
-    t16, r16 = table.to(torch.bfloat16), resid.to(torch.bfloat16)
-    ox16, oy16 = ox.to(torch.bfloat16), oy.to(torch.bfloat16)
-    nb16 = 4 * T * HIDDEN * 2 + T * 4 + HIDDEN * 4
-    timed(lambda: q.native_gather_rms(t16, ids, gam, EPS, add=r16, out_x=ox16, out_y=oy16, ctx=ctx),
-          nb16, "cfg2_gather_residual_rms_bf16")
-    del t16, r16, ox16, oy16, table, resid, ox, oy
-    Qin = torch.randn((T, HQ, HEAD_DIM), generator=g, **f)
-    Kin = torch.randn((T, HKV, HEAD_DIM), generator=g, **f)
-    gq = torch.randn((HEAD_DIM,), generator=g, **f).mul_(0.02)
-    cos, sin = q.rope_table(THETA, ROTARY, SEQ, device=device)
-    Qo, Ko = torch.empty_like(Qin), torch.empty_like(Kin)
-
-    def qk():
-        q.native_qk_norm_rope(Qin, gq, EPS, ROTARY, cos, sin, seq_len=SEQ, out=Qo, ctx=ctx)
-        q.native_qk_norm_rope(Kin, gq, EPS, ROTARY, cos, sin, seq_len=SEQ, out=Ko, ctx=ctx)
-    timed(qk, 2 * (Qin.numel() + Kin.numel()) * 4 + 2 * SEQ * (ROTARY // 2) * 4, "cfg3_qk_norm_rope")
-    del Qin, Kin, Qo, Ko
-    T4 = 32768
-    x = torch.randn((T4, HIDDEN), generator=g, **f)
-    m = torch.randn((T4, HIDDEN), generator=g, **f)
-    rr, yy = torch.empty_like(x), torch.empty_like(x)
-    timed(lambda: q.native_residual_rms(x, m, gam, EPS, out_r=rr, out_y=yy, ctx=ctx),
-          4 * x.numel() * 4 + HIDDEN * 4, "cfg4_post_residual_rms")
-    del x, m, rr, yy
-    gg = torch.randn((T4, INTER), generator=g, **f)
-    uu = torch.randn((T4, INTER), generator=g, **f)
-    h32 = torch.empty_like(gg)
-    h16 = torch.empty((T4, INTER), dtype=torch.bfloat16, device=device)
-    n = gg.numel()
-    timed(lambda: q.native_mlp_gate(gg, uu, out_f32=h32, ctx=ctx), 12 * n, "cfg4_swiglu_f32")
-    timed(lambda: q.native_mlp_gate(gg, uu, want_f32=False, out_bf16=h16, ctx=ctx), 10 * n,
-          "cfg4_swiglu_bf16")
-    timed(lambda: q.native_mlp_gate(gg, uu, out_f32=h32, out_bf16=h16, ctx=ctx), 14 * n,
-          "cfg4_swiglu_f32_and_bf16")
-    del gg, uu, h32, h16
-    torch.cuda.empty_cache()
+        out[label] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
+                      "bytes": nbytes}
+        del fn
+        torch.cuda.empty_cache()
     return out
+
+
+def run_single_kernel(args):
+    """--kernel NAME: one kernel alone (the small cases profiled with ncu)."""
+    import torch
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak, kind = hbm_peak()
+    fn, nbytes = single_kernel(args.kernel, args.tokens, device)
+    us = time_launches(fn, device, args.steps, args.warmup)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "launches": args.warmup + args.steps,
+                      "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
+                      "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "peak": peak,
+                      "peak_kind": kind}), flush=True)
 
 
 # -------------------------------------------------------------- CPU legs
@@ -432,14 +495,20 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-kernel configs 2-4")
+    ap.add_argument("--kernel", default=None,
+                    help="time one kernel alone (gather_rms[_bf16], post_rms[_bf16], swiglu, "
+                         "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope)")
+    ap.add_argument("--tokens", type=int, default=16384, help="rows for --kernel")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and not args.kernel:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_setup(args)
     if args.gpus > 1 and world == 1 and "WORLD_SIZE" not in os.environ:
         reexec_with_torchrun(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.kernel:
+        return run_single_kernel(args)
 
     import torch
     import torch.distributed as dist

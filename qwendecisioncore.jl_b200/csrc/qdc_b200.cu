@@ -59,6 +59,17 @@ int cuda_fail(qdc_ctx* ctx, cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Multiplier and shift of qdc::FastDiv for divisor d >= 1.
+qdc::FastDiv make_fastdiv(uint32_t d) {
+    qdc::FastDiv f;
+    f.d = d < 1 ? 1 : d;
+    uint32_t l = 0;
+    while ((uint64_t(1) << l) < f.d) ++l;
+    f.l = l;
+    f.m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << l) - f.d)) / f.d + 1);
+    return f;
+}
+
 // Switches to the context's device for the duration of a call.
 struct DeviceGuard {
     int prev = -1;
@@ -103,10 +114,22 @@ int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int
     return int(g < 1 ? 1 : g);
 }
 
-template <typename Kernel, typename Args>
-int launch(qdc_ctx* ctx, Kernel kernel, int grid, const Args& args, void* stream, const char* name) {
-    kernel<<<grid, qdc::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(args);
-    cudaError_t e = cudaGetLastError();
+// Launch with programmatic stream serialization (see qdc_kernels.cuh).
+template <typename Args>
+int launch(qdc_ctx* ctx, void (*kernel)(Args), int grid, const Args& args, void* stream,
+           const char* name) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(qdc::kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch %s: %s", name, cudaGetErrorString(e));
     return QDC_OK;
 }
@@ -511,8 +534,13 @@ int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, 
     const int half = rotary / 2;
     bool vec = aligned16(out) && aligned16(in) && in_tok % 4 == 0 && in_head % 4 == 0 &&
                (rotary == 0 || (half % 4 == 0 && aligned16(cos_tab) && aligned16(sin_tab)));
+    // The vector kernel counts units and positions in 32 bits.
+    vec = vec && tokens * heads < (int64_t(1) << 32) - (int64_t(1) << 24);
+    const int64_t period = seq_len > 0 ? seq_len : tokens;
     qdc::HeadArgs a{out, in, nullptr, gamma, cos_tab, sin_tab, eps, heads, dim, rotary,
-                    tokens * heads, in_tok, in_head, 0, 0, int64_t(heads) * dim, pos_offset, seq_len};
+                    tokens * heads, in_tok, in_head, 0, 0, int64_t(heads) * dim, pos_offset, seq_len,
+                    make_fastdiv(uint32_t(heads)),
+                    make_fastdiv(uint32_t(period < (int64_t(1) << 31) ? period : (int64_t(1) << 31)))};
     return launch_heads<false>(ctx, a, vec, stream, "qk_norm_rope");
 }
 
@@ -530,8 +558,10 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
         return fail(ctx, QDC_EINVAL, "leading dimensions too small for heads*dim=%lld", (long long)row_width);
     bool vec = aligned16(out) && aligned16(o) && aligned16(z) && o_ld % 4 == 0 && z_ld % 4 == 0 &&
                z_off % 4 == 0 && out_ld % 4 == 0;
+    vec = vec && rows * heads < (int64_t(1) << 32) - (int64_t(1) << 24);
     qdc::HeadArgs a{out, o, z, gamma, nullptr, nullptr, eps, heads, dim, 0,
-                    rows * heads, o_ld, dim, z_ld, z_off, out_ld, 0, 0};
+                    rows * heads, o_ld, dim, z_ld, z_off, out_ld, 0, 0,
+                    make_fastdiv(uint32_t(heads)), make_fastdiv(1)};
     return launch_heads<true>(ctx, a, vec, stream, "gated_rms");
 }
 

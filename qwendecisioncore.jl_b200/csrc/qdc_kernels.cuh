@@ -27,6 +27,18 @@ namespace qdc {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kThreads = 256;  // 8 warps per CTA for the vector kernels
 
+// ------------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialization: a kernel's CTAs
+// may become resident while its predecessor drains.  Each kernel first waits
+// for the predecessor grid to complete (griddepcontrol.wait -- a no-op when
+// launched without the attribute) and only then touches global memory, then
+// lets its own successor start launching.  This hides the launch and ramp
+// of each of the ~100 kernels of a forward step.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- memory ops
 
 __device__ __forceinline__ float4 ld_nc_f4(const float* p) {
@@ -136,9 +148,47 @@ __device__ __forceinline__ float rms_scale(float sumsq, float width, float eps) 
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, width), eps)));
 }
 
-// silu(x) = x * inv(1 + exp(-x)), src/backbone.jl:196-197 (accurate expf).
+// silu(x) = x * inv(1 + exp(-x)), src/backbone.jl:196-197.  exp(-x) is
+// 2^(-x log2 e) on the SFU (ex2.approx) and the inverse is rcp.approx: two
+// SFU ops instead of an accurate expf plus an IEEE division (~30
+// instructions), which made the SwiGLU and gated-norm kernels issue-bound.
+// Error: ~2 ulp, plus |x| * 6e-8 relative from rounding x*log2(e) -- below
+// 1.2e-6 relative for |x| <= 20 and, beyond that, on outputs far below the
+// 1e-6 absolute tolerance.  Special values follow the reference formula:
+// silu(+-0) = +-0, silu(+inf) = +inf, silu(-inf) = NaN, silu(NaN) = NaN,
+// and large negative x gives a signed zero.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float silu(float x) {
-    return __fmul_rn(x, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))));
+    const float e = ex2_approx(__fmul_rn(x, -1.4426950408889634f));
+    return __fmul_rn(x, rcp_approx(__fadd_rn(1.0f, e)));
+}
+
+// Division of 32-bit unsigned numerators by a divisor fixed at launch, by
+// multiply-high and shift (Granlund & Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994, round-up method):
+//   l = ceil(log2 d),  m = floor(2^32 (2^l - d) / d) + 1,
+//   n / d = (umulhi(m, n) + n) >> l   (the add is done in 64 bits).
+struct FastDiv {
+    uint32_t d, m, l;
+};
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+    return uint32_t((uint64_t(__umulhi(f.m, n)) + n) >> f.l);
+}
+
+__device__ __forceinline__ uint32_t fmod(uint32_t n, const FastDiv& f) {
+    return n - fdiv(n, f) * f.d;
 }
 
 // ------------------------------------------------------------ row kernels
@@ -172,6 +222,7 @@ __device__ __forceinline__ const T* row_source(const RowArgs& a, int64_t row, bo
 // aligned with 16-byte-multiple leading dimensions (checked on the host).
 template <typename T, int CHUNKS>
 __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
+    pdl_enter();
     using C = Chunk<T>;
     constexpr int N = C::N;
     constexpr int W = 32 * N * CHUNKS;
@@ -239,6 +290,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
 // pass re-reads x and m, which are still in L1/L2).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int64_t stride = int64_t(gridDim.x) * warps;
@@ -291,10 +343,13 @@ struct HeadArgs {
     int64_t z_tok, z_off;
     int64_t out_tok;
     int64_t pos_offset, seq_len;
+    FastDiv heads_div;   // unit -> (token, head); units < 2^32 on the vector path
+    FastDiv seq_div;     // token -> position (divisor 1 when seq_len <= 0)
 };
 
 template <int LPU, int CHUNKS, int U, bool GATED>
 __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
+    pdl_enter();
     constexpr int D = 4 * LPU * CHUNKS;
     constexpr int UPW = 32 / LPU;
     __shared__ __align__(16) float gterm[D];
@@ -306,13 +361,14 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
     const int seg = lane / LPU;
     const int l = lane % LPU;
     const int warps = blockDim.x >> 5;
-    const int64_t per_iter = int64_t(UPW) * U;
-    const int64_t stride = int64_t(gridDim.x) * warps * per_iter;
+    const uint32_t per_iter = uint32_t(UPW) * U;
+    const uint32_t units = uint32_t(a.units);
+    const uint32_t stride = gridDim.x * warps * per_iter;
     const int half = a.rotary >> 1;
     const int hl = half >> 2;  // lanes per rotary half
 
-    for (int64_t base = (int64_t(blockIdx.x) * warps + (threadIdx.x >> 5)) * per_iter;
-         base < a.units; base += stride) {
+    for (uint32_t base = (blockIdx.x * warps + (threadIdx.x >> 5)) * per_iter; base < units;
+         base += stride) {
         float4 v[U][CHUNKS];
         float4 zz[GATED ? U : 1][GATED ? CHUNKS : 1];
         int64_t tok[U];
@@ -320,10 +376,11 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
         bool live[U];
 #pragma unroll
         for (int k = 0; k < U; ++k) {
-            const int64_t u = base + int64_t(k) * UPW + seg;
-            live[k] = u < a.units;
-            tok[k] = live[k] ? u / a.heads : 0;
-            hd[k] = live[k] ? int(u - tok[k] * a.heads) : 0;
+            const uint32_t u = base + uint32_t(k * UPW + seg);
+            live[k] = u < units;
+            const uint32_t t = live[k] ? fdiv(u, a.heads_div) : 0u;
+            tok[k] = t;
+            hd[k] = live[k] ? int(u - t * uint32_t(a.heads)) : 0;
             const float* src = a.in + tok[k] * a.in_tok + int64_t(hd[k]) * a.in_head;
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c)
@@ -375,7 +432,7 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
                     p.w = __shfl_sync(kFull, v[k][0].w, partner);
                     if (live[k] && l < 2 * hl) {
                         const int64_t pos =
-                            a.pos_offset + (a.seq_len > 0 ? tok[k] % a.seq_len : tok[k]);
+                            a.pos_offset + int64_t(fmod(uint32_t(tok[k]), a.seq_div));
                         const int j = (l < hl ? l : l - hl) * 4;
                         const float4 cs = ld_nc_f4(a.cos_tab + pos * half + j);
                         const float4 sn = ld_nc_f4(a.sin_tab + pos * half + j);
@@ -407,6 +464,7 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
 // partner is recomputed from its own input element.
 template <bool GATED>
 __global__ void __launch_bounds__(kThreads) head_norm_generic(HeadArgs a) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int64_t stride = int64_t(gridDim.x) * warps;
@@ -464,6 +522,7 @@ struct SwigluArgs {
 // Warp per row, 4 x 16-byte loads of g and of u in flight per lane.
 template <bool F32, bool BF16>
 __global__ void __launch_bounds__(kThreads) swiglu_vec(SwigluArgs a) {
+    pdl_enter();
     constexpr int U = 4;
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
@@ -503,6 +562,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_vec(SwigluArgs a) {
 }
 
 __global__ void __launch_bounds__(kThreads) swiglu_generic(SwigluArgs a) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int64_t stride = int64_t(gridDim.x) * warps;

@@ -1,0 +1,196 @@
+# QwenDecisionCoreB200Ext -- binds libqdc_b200.so into QwenDecisionCore.jl.
+#
+# A package extension of QwenDecisionCore.jl (declare it in Project.toml
+# [extensions] next to QwenDecisionCoreCUDAExt, triggered by CUDA).  It keeps
+# every CUDA.jl array, cuBLAS GEMM, attention and DeltaNet path of
+# QwenDecisionCoreCUDAExt and replaces only the per-layer row kernels --
+# gather, RMSNorm (+ residual), q/k norm + partial RoPE, gated RMSNorm,
+# SwiGLU -- by `ccall`s into libqdc_b200.so (include/qdc_b200.h).
+#
+# Selection.  QwenBackbone(dir; device = :cuda) loads CuArrays exactly as
+# before; when the active device is a compute capability 10.0 GPU and the
+# library loads, `use_b200()` is true and the hooks below run the sm_100a
+# kernels.  The CUDA extension's own kernels are not redefined: its
+# `native_*` methods dispatch here through the `B200Kernels` hook table
+# that the maintainer adds to ext/cuda_workspace.jl (see INTEGRATION.md, the
+# five call sites are listed there), so no method is overwritten.
+#
+# NOTE: Julia is not installed in the environment this library was built
+# and tested in; this file is the binding a maintainer adds, exercised there
+# only through its Python twin (qdc_b200/_lib.py), which calls the same
+# entry points with the same arguments.
+module QwenDecisionCoreB200Ext
+
+import QwenDecisionCore
+import CUDA
+
+const QDC = QwenDecisionCore
+const LIB = get(ENV, "QDC_B200_LIB", joinpath(@__DIR__, "..", "deps", "libqdc_b200.so"))
+
+const QDC_OK = Cint(0)
+const QDC_EINVAL = Cint(1)
+const QDC_EBOUNDS = Cint(2)
+const QDC_F32 = Cint(0)
+const QDC_BF16 = Cint(1)
+
+# ---------------------------------------------------------------- context
+
+mutable struct Context
+    handle::Ptr{Cvoid}
+end
+
+const CONTEXTS = Dict{Int,Context}()
+const CONTEXT_LOCK = ReentrantLock()
+
+function check(status::Cint, handle::Ptr{Cvoid} = C_NULL)
+    status == QDC_OK && return nothing
+    msg = unsafe_string(ccall((:qdc_last_error, LIB), Cstring, (Ptr{Cvoid},), handle))
+    # src/backbone.jl:413-422 raises ArgumentError for bad ids and shapes
+    status in (QDC_EINVAL, QDC_EBOUNDS) && throw(ArgumentError(msg))
+    error("libqdc_b200: " * msg)
+end
+
+function context(dev::CUDA.CuDevice = CUDA.device())
+    key = CUDA.deviceid(dev)
+    lock(CONTEXT_LOCK) do
+        get!(CONTEXTS, key) do
+            ref = Ref{Ptr{Cvoid}}(C_NULL)
+            check(ccall((:qdc_init, LIB), Cint, (Cint, Ptr{Ptr{Cvoid}}), Cint(key), ref))
+            ctx = Context(ref[])
+            finalizer(c -> ccall((:qdc_destroy, LIB), Cint, (Ptr{Cvoid},), c.handle), ctx)
+            ctx
+        end
+    end
+end
+
+use_b200() = CUDA.functional() && CUDA.capability(CUDA.device()) == v"10.0" && isfile(LIB)
+
+stream_handle() = Base.unsafe_convert(Ptr{Cvoid}, CUDA.stream().handle)
+ptr(x::CUDA.CuArray) = Base.unsafe_convert(Ptr{Cvoid}, pointer(x))
+ptr(::Nothing) = C_NULL
+ld(x::CUDA.CuArray) = Int64(size(x, 1))  # column stride of a dense Julia matrix
+
+# ------------------------------------------------------------- entry points
+# Julia (width, tokens) column-major == [tokens][width] row-major: the
+# leading dimension of the C ABI is the Julia column stride.
+
+"""residual_rms!(out_r, out_y, x, m, weight, eps; centered=true)
+
+r = x + m (stored in out_r unless it is nothing), y = rms(r) .* (1 .+ w)
+(or .* w).  `m === nothing`: plain RMSNorm (src/backbone.jl:200-204)."""
+function residual_rms!(out_r, out_y::CUDA.CuArray{Float32}, x::CUDA.CuArray{Float32}, m, weight,
+                       eps; centered::Bool = true)
+    width = size(x, 1)
+    rows = length(x) ÷ width
+    ctx = context()
+    check(ccall((:qdc_residual_rms, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Cfloat,
+                 Cint, Int64, Int64, Int64, Int64, Int64, Int64, Cint, Ptr{Cvoid}),
+                ctx.handle, ptr(out_r), ptr(out_y), ptr(x), ptr(m), ptr(weight), Float32(eps),
+                Cint(centered), Int64(rows), Int64(width), Int64(width), Int64(width),
+                Int64(width), Int64(width), QDC_F32, stream_handle()), ctx.handle)
+    return out_y
+end
+
+"""gather_rms!(out_x, out_y, embedding, ids, weight, eps)
+
+out_x[:, t] = embedding[:, ids[t]+1]; out_y = rms(out_x) (weight nothing:
+gather only).  ids are host integers, validated and staged by the library."""
+function gather_rms!(out_x, out_y, embedding::CUDA.CuMatrix{Float32}, ids::Vector{<:Integer},
+                     weight, eps)
+    hidden, vocab = size(embedding)
+    host = Int32.(ids)
+    ctx = context()
+    check(ccall((:qdc_gather_rms, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Int32}, Ptr{Cvoid}, Ptr{Cvoid},
+                 Cfloat, Cint, Int64, Int64, Int64, Cint, Ptr{Cvoid}),
+                ctx.handle, ptr(out_x), ptr(out_y), ptr(embedding), host, C_NULL, ptr(weight),
+                Float32(eps), Cint(1), Int64(length(host)), Int64(hidden), Int64(vocab), QDC_F32,
+                stream_handle()), ctx.handle)
+    return out_x, out_y
+end
+
+"""qk_norm_rope!(out, projected, weight, eps, rotary, cos, sin; source_width, offset)
+
+Per-head RMSNorm (1+w) and rotate-half RoPE on the first `rotary` dims of
+each head of `projected` (head h of token t at rows (h-1)*source_width .+
+(1:dim) of column t: source_width = 2dim for the packed [q; gate] query
+projection, dim for keys).  `out` is (dim, heads, tokens)."""
+function qk_norm_rope!(out::CUDA.CuArray{Float32,3}, projected::CUDA.CuMatrix{Float32}, weight,
+                       eps, rotary::Integer, cos::CUDA.CuMatrix{Float32},
+                       sin::CUDA.CuMatrix{Float32}; source_width::Integer, offset::Integer = 0)
+    dim, heads, tokens = size(out)
+    ctx = context()
+    check(ccall((:qdc_qk_norm_rope, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Cint, Cint, Int64, Int64, Ptr{Cvoid},
+                 Cfloat, Cint, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Int64, Int64, Ptr{Cvoid}),
+                ctx.handle, ptr(out), ptr(projected), Int64(tokens), Cint(heads), Cint(dim),
+                Int64(size(projected, 1)), Int64(source_width), ptr(weight), Float32(eps),
+                Cint(rotary), ptr(cos), ptr(sin), Int64(size(cos, 2)), Int64(offset), Int64(0),
+                stream_handle()), ctx.handle)
+    return out
+end
+
+"""rope_tables(theta, rotary, n) -> (cos, sin) as (rotary/2, n) CuMatrices,
+built on the host exactly as src/backbone_cpu.jl:90-105."""
+function rope_tables(theta::Float32, rotary::Integer, n::Integer)
+    half = rotary ÷ 2
+    c = Matrix{Float32}(undef, half, n)
+    s = Matrix{Float32}(undef, half, n)
+    check(ccall((:qdc_rope_table, LIB), Cint, (Cfloat, Cint, Int64, Ptr{Float32}, Ptr{Float32}),
+                theta, Cint(rotary), Int64(n), c, s))
+    return CUDA.CuArray(c), CUDA.CuArray(s)
+end
+
+"""gated_rms!(out, o, projected, weight, eps; z_offset)
+
+normalized(o) .* w .* silu(z) per (value head, token); z read in place from
+rows z_offset .+ (1:heads*dim) of `projected` (ext/cuda_delta.jl:232-241)."""
+function gated_rms!(out::CUDA.CuMatrix{Float32}, o::CUDA.CuArray{Float32,3},
+                    projected::CUDA.CuMatrix{Float32}, weight, eps; z_offset::Integer)
+    dim, heads, tokens = size(o)
+    ctx = context()
+    check(ccall((:qdc_gated_rms, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Cint, Cint, Int64, Int64,
+                 Int64, Int64, Ptr{Cvoid}, Cfloat, Ptr{Cvoid}),
+                ctx.handle, ptr(out), ptr(o), ptr(projected), Int64(tokens), Cint(heads), Cint(dim),
+                Int64(dim * heads), Int64(size(projected, 1)), Int64(z_offset), Int64(size(out, 1)),
+                ptr(weight), Float32(eps), stream_handle()), ctx.handle)
+    return out
+end
+
+"""swiglu!(out, packed)  -- out = silu(gate) .* up with gate = packed[1:I, :],
+up = packed[I+1:2I, :] (ext/cuda_mlp.jl:63-71)."""
+function swiglu!(out::CUDA.CuMatrix{Float32}, packed::CUDA.CuMatrix{Float32})
+    width = size(out, 1)
+    rows = size(out, 2)
+    ctx = context()
+    gate = ptr(packed)
+    up = gate + width * sizeof(Float32)
+    check(ccall((:qdc_swiglu, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Int64, Int64,
+                 Int64, Int64, Ptr{Cvoid}),
+                ctx.handle, ptr(out), C_NULL, gate, up, Int64(rows), Int64(width),
+                Int64(size(packed, 1)), Int64(size(packed, 1)), Int64(width), stream_handle()),
+          ctx.handle)
+    return out
+end
+
+"""sync!() -- the synchronize of native_forward_scope's `finally`
+(ext/cuda_workspace.jl:62-66), reporting device-side id errors."""
+sync!() = check(ccall((:qdc_sync, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}), context().handle,
+                      stream_handle()), context().handle)
+
+# --------------------------------------------------------------- hook table
+# ext/cuda_workspace.jl gains `const B200Kernels = Ref{Any}(nothing)` and
+# routes its five row-kernel call sites through it when set.
+function __init__()
+    if use_b200()
+        cuda_ext = Base.get_extension(QDC, :QwenDecisionCoreCUDAExt)
+        cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!,
+                                                          qk_norm_rope!, rope_tables, gated_rms!,
+                                                          swiglu!, sync!))
+    end
+end
+
+end # module

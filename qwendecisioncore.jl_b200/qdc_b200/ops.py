@@ -319,7 +319,7 @@ def native_qk_norm_rope(x, weight, eps, rotary, cos, sin, *, pos_offset=0, seq_l
     Position of token t: pos_offset + t % seq_len (seq_len None: t).
     Returns dense (tokens, heads, dim)."""
     dev = _cuda(x, weight, cos, sin, out)
-    if x.dim() != 3 or (x.shape[2] > 1 and x.stride(2) != 1):
+    if x.dim() != 3 or (x.numel() and x.shape[2] > 1 and x.stride(2) != 1):
         raise DimensionMismatch(_lib.QDC_EINVAL, "x must be (tokens, heads, dim) with unit inner stride")
     if x.dtype != torch.float32:
         raise ArgumentError(_lib.QDC_EINVAL, "q/k norm takes Float32 projections")
@@ -360,7 +360,7 @@ def native_gated_rms(o, z, weight, eps, *, out=None, ctx=None, stream=None):
     for t, name in ((o, "o"), (z, "z")):
         if t.dtype != torch.float32:
             raise ArgumentError(_lib.QDC_EINVAL, f"{name} must be Float32")
-        if (dim > 1 and t.stride(2) != 1) or (heads > 1 and t.stride(1) != dim):
+        if t.numel() and ((dim > 1 and t.stride(2) != 1) or (heads > 1 and t.stride(1) != dim)):
             raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} needs contiguous heads within a row")
     weight = _gamma(weight, dim, dev)
     if out is None:

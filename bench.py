@@ -61,15 +61,14 @@ B = 4
 BYTES = {
     "gather_rms": 3 * HIDDEN * B,              # E row read, x and y written
     "gated_rms": 3 * HV * DV * B,              # o, z read; y written
-    "q_norm_rope": 2 * HQ * HEAD_DIM * B,      # q half of [q;gate] read, q written
-    "k_norm_rope": 2 * HKV * HEAD_DIM * B,
+    "qk_norm_rope": 2 * (HQ + HKV) * HEAD_DIM * B,  # q half of [q;gate] and k read, q and k written
     "post_rms": 4 * HIDDEN * B,                # x, m read; r, y written
     "swiglu": 3 * INTER * B,                   # gate, up read; h written
     "mlp_rms": 4 * HIDDEN * B,                 # r, mlp read; r (in place), y written
     "final_rms": 3 * HIDDEN * B,               # r, mlp read; y written
 }
 BYTES_PER_TOKEN = (BYTES["gather_rms"] + 18 * BYTES["gated_rms"]
-                   + 6 * (BYTES["q_norm_rope"] + BYTES["k_norm_rope"]) + 24 * BYTES["post_rms"]
+                   + 6 * BYTES["qk_norm_rope"] + 24 * BYTES["post_rms"]
                    + 24 * BYTES["swiglu"] + 23 * BYTES["mlp_rms"] + BYTES["final_rms"])
 assert BYTES_PER_TOKEN == 2_392_064
 
@@ -176,8 +175,11 @@ class LayerKernelStep:
         self.gate_up = normal((T, 2 * INTER))
         self.delta_o = normal((T, HV, DV))
         self.delta_proj = normal((T, PROJ_W))
-        self.qgate = normal((T, HQ, 2 * HEAD_DIM))
-        self.k_raw = normal((T, HKV, HEAD_DIM))
+        # packed [q;gate | k | v] attention projection (ext/cuda_mlp.jl:13)
+        self.attn_proj = normal((T, HQ * 2 * HEAD_DIM + 2 * HKV * HEAD_DIM))
+        self.qgate = self.attn_proj[:, :HQ * 2 * HEAD_DIM].view(T, HQ, 2 * HEAD_DIM)
+        self.k_raw = self.attn_proj[:, HQ * 2 * HEAD_DIM:HQ * 2 * HEAD_DIM + HKV * HEAD_DIM].view(
+            T, HKV, HEAD_DIM)
         # kernel outputs
         self.x = torch.empty((T, HIDDEN), **f)
         self.r = torch.empty((T, HIDDEN), **f)
@@ -190,8 +192,7 @@ class LayerKernelStep:
         torch.cuda.synchronize(device)
 
     def launches(self, include_gather=True):
-        n = sum(2 if k == "full" else 1 for k in KINDS) + 3 * LAYERS
-        return n + (1 if include_gather else 0)
+        return step_launches() - (0 if include_gather else 1)
 
     def bytes(self):
         return self.T * BYTES_PER_TOKEN
@@ -213,12 +214,10 @@ class LayerKernelStep:
                                    ctx=ctx)
                 tick("gated_rms")
             else:
-                q.native_qk_norm_rope(self.qgate[:, :, :HEAD_DIM], self.q_norm[layer], EPS, ROTARY,
-                                      self.cos, self.sin, seq_len=SEQ, out=self.q_out, ctx=ctx)
-                tick("q_norm_rope")
-                q.native_qk_norm_rope(self.k_raw, self.k_norm[layer], EPS, ROTARY, self.cos,
-                                      self.sin, seq_len=SEQ, out=self.k_out, ctx=ctx)
-                tick("k_norm_rope")
+                q.native_q_k_norm_rope(self.qgate[:, :, :HEAD_DIM], self.k_raw, self.q_norm[layer],
+                                       self.k_norm[layer], EPS, ROTARY, self.cos, self.sin,
+                                       seq_len=SEQ, q_out=self.q_out, k_out=self.k_out, ctx=ctx)
+                tick("qk_norm_rope")
             q.native_residual_rms(x, self.m, self.post_norm[layer], EPS, out_r=r, out_y=self.y,
                                   ctx=ctx)
             tick("post_rms")
@@ -313,9 +312,9 @@ def single_kernel(name, tokens, device, seed=1):
             return kn, 2 * ko.numel() * 4 + table
 
         def both():
-            qn()
-            kn()
-        return both, 2 * (qo.numel() + ko.numel()) * 4 + 2 * table
+            q.native_q_k_norm_rope(qgate[:, :, :HEAD_DIM], kin, gq, gq, EPS, ROTARY, cos, sin,
+                                   seq_len=SEQ, q_out=qo, k_out=ko, ctx=ctx)
+        return both, 2 * (qo.numel() + ko.numel()) * 4 + table
     raise SystemExit(f"unknown kernel {name}")
 
 
@@ -375,6 +374,43 @@ def run_single_kernel(args):
                       "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "peak": peak,
                       "peak_kind": kind}), flush=True)
+
+
+# ------------------------------------------------------------- forward leg
+
+def config5():
+    """the 0.8B-shaped hybrid backbone."""
+    from qdc_b200.model import Config
+    return Config(hidden=HIDDEN, head_dim=HEAD_DIM, heads=HQ, kv_heads=HKV, key_heads=HK,
+                  value_heads=HV, key_dim=DK, value_dim=DV, eps=float(EPS), rope_theta=THETA,
+                  rotary_dim=ROTARY, vocab=VOCAB, intermediate=INTER, layer_types=[
+                      "linear_attention" if k == "delta" else "full_attention" for k in KINDS])
+
+
+def forward_leg(world, rank, device, seqs, steps, warmup, max_over_ranks):
+    """Forward tokens/sec of the whole config-5 forward (random-init weights,
+    Float32): the rank's sequences through QwenBackbone.batch_hidden, every
+    per-layer op on the qdc kernels, projections / attention / DeltaNet as
+    torch Float32 stand-ins."""
+    import numpy as np
+    import torch
+    import qdc_b200 as q
+    model = q.QwenBackbone.random(config5(), seed=0, device=device)
+    rng = np.random.default_rng(100 + rank)
+    ids = rng.integers(0, VOCAB, (seqs, SEQ))
+    for _ in range(warmup):
+        model.batch_hidden(ids)
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        model.batch_hidden(ids)
+    e.record()
+    torch.cuda.synchronize(device)
+    ms = max_over_ranks(s.elapsed_time(e)) / steps
+    del model
+    torch.cuda.empty_cache()
+    return ms
 
 
 # -------------------------------------------------------------- CPU legs
@@ -499,6 +535,8 @@ def main():
                     help="time one kernel alone (gather_rms[_bf16], post_rms[_bf16], swiglu, "
                          "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope)")
     ap.add_argument("--tokens", type=int, default=16384, help="rows for --kernel")
+    ap.add_argument("--no-forward", action="store_true", help="skip the whole-forward tokens/s leg")
+    ap.add_argument("--forward-steps", type=int, default=2)
     args = ap.parse_args()
     if args.warmup < 3 and not args.kernel:
         ap.error("--warmup must be >= 3")
@@ -635,16 +673,26 @@ def main():
     e2e_ms = max_over_ranks(e_s.elapsed_time(e_e)) / args.steps
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
 
+    # --- whole forward (every rank; config-5 sequences sharded) ------------
+    step_bytes = step.bytes()
+    del graph, rest, inst, step, host_out, e2e_step
+    torch.cuda.empty_cache()
+    forward = None
+    if not args.no_forward:
+        fwd_ms = forward_leg(world, rank, device, seqs, args.forward_steps, 1, max_over_ranks)
+        forward = {"tokens_per_s": round(SEQS * SEQ / (fwd_ms * 1e-3), 1),
+                   "ms_per_forward": round(fwd_ms, 3), "forwards": args.forward_steps,
+                   "layer_kernel_ms": round(ms, 3),
+                   "layer_kernel_share": round(ms / fwd_ms, 4),
+                   "what": "QwenBackbone.batch_hidden over the rank's config-5 sequences: qdc "
+                           "per-layer kernels + torch Float32 GEMMs (TF32 off), SDPA attention and "
+                           "chunked gated delta rule as the out-of-scope stand-ins; random-init "
+                           "weights; device-event time, max over ranks"}
+
     # --- BASELINE per-kernel configs (rank 0 GPU) -------------------------
     configs = None
     if rank == 0 and not args.no_configs:
-        del graph, rest, inst
-        step_bytes = step.bytes()
-        del step
-        torch.cuda.empty_cache()
         configs = kernel_configs(device, peak)
-    else:
-        step_bytes = step.bytes()
 
     # --- CPU baseline (rank 0 at N=1) -------------------------------------
     cpu = None
@@ -695,6 +743,8 @@ def main():
             "gpu_launches": args.steps * step_launches(),
             "clocks": clock_info,
         }
+        if forward is not None:
+            line["forward"] = forward
         if configs is not None:
             line["configs"] = configs
         if cpu is not None:
@@ -706,7 +756,7 @@ def main():
 
 
 def step_launches():
-    return 1 + sum(2 if k == "full" else 1 for k in KINDS) + 3 * LAYERS
+    return 1 + len(KINDS) + 3 * LAYERS
 
 
 if __name__ == "__main__":

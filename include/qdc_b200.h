@@ -168,6 +168,23 @@ QDC_API int qdc_qk_norm_rope(qdc_ctx *ctx, float *out, const float *in,
                      int64_t table_rows, int64_t pos_offset, int64_t seq_len,
                      void *stream);
 
+/* qdc_qk_norm_rope for the query AND key heads of the same tokens in one
+ * launch: q head h of token t at q_in + t*q_tok + h*q_head, k head h at
+ * k_in + t*k_tok + h*k_head; outputs dense [tokens][q_heads][dim] and
+ * [tokens][k_heads][dim]; q_gamma / k_gamma are the two centered gammas.
+ * Replaces the two prepare_head_kernel! launches of full_attention
+ * (ext/cuda_attention.jl:128,141); the key heads then cost no launch of
+ * their own. */
+QDC_API int qdc_q_k_norm_rope(qdc_ctx *ctx, float *q_out, float *k_out,
+                              const float *q_in, const float *k_in,
+                              int64_t tokens, int q_heads, int k_heads, int dim,
+                              int64_t q_tok, int64_t q_head, int64_t k_tok,
+                              int64_t k_head, const float *q_gamma,
+                              const float *k_gamma, float eps, int rotary,
+                              const float *cos_tab, const float *sin_tab,
+                              int64_t table_rows, int64_t pos_offset,
+                              int64_t seq_len, void *stream);
+
 /* Gated RMSNorm of the Gated DeltaNet output:  y = ((o*s)*g)*silu(z),
  * uncentered gamma (src/backbone.jl:339-341, src/backbone_cpu.jl:750-755).
  * o head h of row t at o + t*o_ld + h*dim; z at z + t*z_ld + z_off + h*dim

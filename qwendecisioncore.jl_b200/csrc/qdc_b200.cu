@@ -106,11 +106,18 @@ int resident_blocks(const void* kernel, int device, int threads) {
     return n;
 }
 
-// Persistent grid: enough CTAs for the work, at most one full wave.
+// Persistent grid of at most one full wave, balanced: with R grid-stride
+// rounds needed at full occupancy, launch just enough CTAs that every round
+// is full except the last few units, so no round runs with a fraction of the
+// warps (at 8192 rows a full wave of 3552 warps would leave the third round
+// 31% busy).
 int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units) {
-    const int64_t wanted = (units + work_per_block_units - 1) / work_per_block_units;
     const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, qdc::kThreads);
-    int64_t g = wanted < cap ? wanted : cap;
+    const int64_t per_wave = cap * work_per_block_units;
+    const int64_t rounds = (units + per_wave - 1) / per_wave;
+    const int64_t per_block = rounds * work_per_block_units;
+    int64_t g = (units + per_block - 1) / per_block;
+    if (g > cap) g = cap;
     return int(g < 1 ? 1 : g);
 }
 
@@ -145,14 +152,14 @@ RowKernel<T> row_vec_kernel(int64_t chunks);
 template <>
 RowKernel<float> row_vec_kernel<float>(int64_t chunks) {
     switch (chunks) {
-        case 1: return qdc::row_rms_vec<float, 1>;
-        case 2: return qdc::row_rms_vec<float, 2>;
-        case 3: return qdc::row_rms_vec<float, 3>;
-        case 4: return qdc::row_rms_vec<float, 4>;
-        case 6: return qdc::row_rms_vec<float, 6>;
-        case 8: return qdc::row_rms_vec<float, 8>;
-        case 12: return qdc::row_rms_vec<float, 12>;
-        case 16: return qdc::row_rms_vec<float, 16>;
+        case 1: return qdc::row_rms_vec<float, 1, 1>;
+        case 2: return qdc::row_rms_vec<float, 2, 1>;
+        case 3: return qdc::row_rms_vec<float, 3, 1>;
+        case 4: return qdc::row_rms_vec<float, 4, 1>;
+        case 6: return qdc::row_rms_vec<float, 6, 1>;
+        case 8: return qdc::row_rms_vec<float, 8, 1>;
+        case 12: return qdc::row_rms_vec<float, 12, 1>;
+        case 16: return qdc::row_rms_vec<float, 16, 1>;
         default: return nullptr;
     }
 }
@@ -160,14 +167,14 @@ RowKernel<float> row_vec_kernel<float>(int64_t chunks) {
 template <>
 RowKernel<uint16_t> row_vec_kernel<uint16_t>(int64_t chunks) {
     switch (chunks) {
-        case 1: return qdc::row_rms_vec<uint16_t, 1>;
-        case 2: return qdc::row_rms_vec<uint16_t, 2>;
-        case 3: return qdc::row_rms_vec<uint16_t, 3>;
-        case 4: return qdc::row_rms_vec<uint16_t, 4>;
-        case 6: return qdc::row_rms_vec<uint16_t, 6>;
-        case 8: return qdc::row_rms_vec<uint16_t, 8>;
-        case 12: return qdc::row_rms_vec<uint16_t, 12>;
-        case 16: return qdc::row_rms_vec<uint16_t, 16>;
+        case 1: return qdc::row_rms_vec<uint16_t, 1, 1>;
+        case 2: return qdc::row_rms_vec<uint16_t, 2, 1>;
+        case 3: return qdc::row_rms_vec<uint16_t, 3, 1>;
+        case 4: return qdc::row_rms_vec<uint16_t, 4, 1>;
+        case 6: return qdc::row_rms_vec<uint16_t, 6, 1>;
+        case 8: return qdc::row_rms_vec<uint16_t, 8, 1>;
+        case 12: return qdc::row_rms_vec<uint16_t, 12, 1>;
+        case 16: return qdc::row_rms_vec<uint16_t, 16, 1>;
         default: return nullptr;
     }
 }
@@ -480,7 +487,7 @@ HeadKernel head_vec_kernel(int dim, int* lpu) {
         case 32: *lpu = 8; return qdc::head_norm_vec<8, 1, 4, GATED>;
         case 64: *lpu = 16; return qdc::head_norm_vec<16, 1, 4, GATED>;
         case 128: *lpu = 32; return qdc::head_norm_vec<32, 1, 4, GATED>;
-        case 256: *lpu = 32; return qdc::head_norm_vec<32, 2, 2, GATED>;
+        case 256: *lpu = 32; return qdc::head_norm_vec<32, 2, 1, GATED>;
         case 512: *lpu = 32; return qdc::head_norm_vec<32, 4, 1, GATED>;
         default: return nullptr;
     }
@@ -499,7 +506,7 @@ int launch_heads(qdc_ctx* ctx, const qdc::HeadArgs& a, bool vec_ok, void* stream
         k = qdc::head_norm_generic<GATED>;
         units_per_block = qdc::kThreads / 32;
     } else {
-        const int unroll = a.dim == 256 ? 2 : (a.dim == 512 ? 1 : 4);
+        const int unroll = a.dim >= 256 ? 1 : 4;  // must match head_vec_kernel's U
         units_per_block = int64_t(qdc::kThreads / 32) * (32 / lpu) * unroll;
     }
     const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), units_per_block, a.units);
@@ -510,21 +517,31 @@ int launch_heads(qdc_ctx* ctx, const qdc::HeadArgs& a, bool vec_ok, void* stream
 
 extern "C" {
 
-int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, int heads, int dim,
-                     int64_t in_tok, int64_t in_head, const float* gamma, float eps, int rotary,
-                     const float* cos_tab, const float* sin_tab, int64_t table_rows, int64_t pos_offset,
-                     int64_t seq_len, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// q/k norm + RoPE of one head group (k_heads == 0) or of the query and key
+// groups of the same tokens in one launch.
+int qk_impl(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const float* k_in,
+            int64_t tokens, int q_heads, int k_heads, int dim, int64_t q_tok, int64_t q_head,
+            int64_t k_tok, int64_t k_head, const float* q_gamma, const float* k_gamma, float eps,
+            int rotary, const float* cos_tab, const float* sin_tab, int64_t table_rows,
+            int64_t pos_offset, int64_t seq_len, void* stream) {
     if (int s = check_ctx(ctx)) return s;
-    if (tokens < 0 || heads < 1 || dim < 1 || dim > 8192)
-        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d dim=%d", (long long)tokens, heads, dim);
+    if (tokens < 0 || q_heads < 1 || k_heads < 0 || dim < 1 || dim > 8192)
+        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d+%d dim=%d", (long long)tokens,
+                    q_heads, k_heads, dim);
     if (rotary < 0 || (rotary & 1) || rotary > dim)
         return fail(ctx, QDC_EINVAL, "rotary=%d must be even and <= dim=%d", rotary, dim);
     if (tokens == 0) return QDC_OK;
-    if (out == nullptr || in == nullptr || gamma == nullptr)
+    if (q_out == nullptr || q_in == nullptr || q_gamma == nullptr)
         return fail(ctx, QDC_EINVAL, "out, in and gamma are required");
-    if (in_tok < 0 || in_head < 0) return fail(ctx, QDC_EINVAL, "negative stride");
+    if (k_heads > 0 && (k_out == nullptr || k_in == nullptr || k_gamma == nullptr))
+        return fail(ctx, QDC_EINVAL, "k_out, k_in and k_gamma are required");
+    if (q_tok < 0 || q_head < 0 || k_tok < 0 || k_head < 0) return fail(ctx, QDC_EINVAL, "negative stride");
     if (pos_offset < 0) return fail(ctx, QDC_EINVAL, "negative position offset");
-    if (rotary > 0 && tokens > 0) {
+    if (rotary > 0) {
         if (cos_tab == nullptr || sin_tab == nullptr) return fail(ctx, QDC_EINVAL, "RoPE tables are NULL");
         const int64_t span = seq_len > 0 ? (tokens < seq_len ? tokens : seq_len) : tokens;
         if (pos_offset + span - 1 >= table_rows)
@@ -532,16 +549,43 @@ int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, 
                         (long long)(pos_offset + span - 1), (long long)table_rows);
     }
     const int half = rotary / 2;
-    bool vec = aligned16(out) && aligned16(in) && in_tok % 4 == 0 && in_head % 4 == 0 &&
+    const int64_t units = tokens * (q_heads + k_heads);
+    bool vec = aligned16(q_out) && aligned16(q_in) && q_tok % 4 == 0 && q_head % 4 == 0 &&
+               (k_heads == 0 || (aligned16(k_out) && aligned16(k_in) && k_tok % 4 == 0 &&
+                                 k_head % 4 == 0)) &&
                (rotary == 0 || (half % 4 == 0 && aligned16(cos_tab) && aligned16(sin_tab)));
     // The vector kernel counts units and positions in 32 bits.
-    vec = vec && tokens * heads < (int64_t(1) << 32) - (int64_t(1) << 24);
+    vec = vec && units < (int64_t(1) << 32) - (int64_t(1) << 24);
     const int64_t period = seq_len > 0 ? seq_len : tokens;
-    qdc::HeadArgs a{out, in, nullptr, gamma, cos_tab, sin_tab, eps, heads, dim, rotary,
-                    tokens * heads, in_tok, in_head, 0, 0, int64_t(heads) * dim, pos_offset, seq_len,
-                    make_fastdiv(uint32_t(heads)),
+    qdc::HeadArgs a{q_out, k_out, q_in, k_in, nullptr, q_gamma, k_gamma, cos_tab, sin_tab, eps,
+                    q_heads, k_heads, dim, rotary, units, q_tok, q_head, k_tok, k_head, 0, 0,
+                    int64_t(q_heads) * dim, int64_t(k_heads) * dim, pos_offset, seq_len,
+                    make_fastdiv(uint32_t(q_heads + k_heads)),
                     make_fastdiv(uint32_t(period < (int64_t(1) << 31) ? period : (int64_t(1) << 31)))};
     return launch_heads<false>(ctx, a, vec, stream, "qk_norm_rope");
+}
+
+}  // namespace
+
+extern "C" {
+
+int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, int heads, int dim,
+                     int64_t in_tok, int64_t in_head, const float* gamma, float eps, int rotary,
+                     const float* cos_tab, const float* sin_tab, int64_t table_rows, int64_t pos_offset,
+                     int64_t seq_len, void* stream) {
+    return qk_impl(ctx, out, nullptr, in, nullptr, tokens, heads, 0, dim, in_tok, in_head, 0, 0, gamma,
+                   nullptr, eps, rotary, cos_tab, sin_tab, table_rows, pos_offset, seq_len, stream);
+}
+
+int qdc_q_k_norm_rope(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const float* k_in,
+                      int64_t tokens, int q_heads, int k_heads, int dim, int64_t q_tok, int64_t q_head,
+                      int64_t k_tok, int64_t k_head, const float* q_gamma, const float* k_gamma,
+                      float eps, int rotary, const float* cos_tab, const float* sin_tab,
+                      int64_t table_rows, int64_t pos_offset, int64_t seq_len, void* stream) {
+    if (k_heads < 1) return fail(ctx, QDC_EINVAL, "k_heads must be >= 1");
+    return qk_impl(ctx, q_out, k_out, q_in, k_in, tokens, q_heads, k_heads, dim, q_tok, q_head, k_tok,
+                   k_head, q_gamma, k_gamma, eps, rotary, cos_tab, sin_tab, table_rows, pos_offset,
+                   seq_len, stream);
 }
 
 int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int64_t rows, int heads,
@@ -559,8 +603,8 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
     bool vec = aligned16(out) && aligned16(o) && aligned16(z) && o_ld % 4 == 0 && z_ld % 4 == 0 &&
                z_off % 4 == 0 && out_ld % 4 == 0;
     vec = vec && rows * heads < (int64_t(1) << 32) - (int64_t(1) << 24);
-    qdc::HeadArgs a{out, o, z, gamma, nullptr, nullptr, eps, heads, dim, 0,
-                    rows * heads, o_ld, dim, z_ld, z_off, out_ld, 0, 0,
+    qdc::HeadArgs a{out, nullptr, o, nullptr, z, gamma, nullptr, nullptr, nullptr, eps, heads, 0, dim,
+                    0, rows * heads, o_ld, dim, 0, 0, z_ld, z_off, out_ld, 0, 0, 0,
                     make_fastdiv(uint32_t(heads)), make_fastdiv(1)};
     return launch_heads<true>(ctx, a, vec, stream, "gated_rms");
 }

@@ -41,9 +41,11 @@ __device__ __forceinline__ void pdl_enter() {
 
 // ---------------------------------------------------------------- memory ops
 
+// Streaming loads: read-only path, no L1 allocation (each byte is read once;
+// measured +3% over plain ld.global.nc on the residual-norm rows).
 __device__ __forceinline__ float4 ld_nc_f4(const float* p) {
     float4 v;
-    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                  : "l"(p));
     return v;
@@ -51,7 +53,7 @@ __device__ __forceinline__ float4 ld_nc_f4(const float* p) {
 
 __device__ __forceinline__ uint4 ld_nc_u4(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
@@ -90,32 +92,36 @@ __device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
     return bf16_bits(lo) | (bf16_bits(hi) << 16);
 }
 
-// A 16-byte chunk of a row: 4 Float32 or 8 bf16 values, held as Float32.
+// A 16-byte chunk of a row (4 Float32 or 8 bf16 values) as loaded: the raw
+// bits stay packed in 4 registers while in flight and are widened to Float32
+// only when used, so bf16 rows keep as many bytes in flight per register as
+// Float32 rows.
 template <typename T> struct Chunk;
 
 template <> struct Chunk<float> {
     static constexpr int N = 4;
-    float v[4];
-    __device__ __forceinline__ void load(const float* p) {
-        float4 t = ld_nc_f4(p);
-        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    uint4 raw;
+    __device__ __forceinline__ void load(const float* p) { raw = ld_nc_u4(p); }
+    __device__ __forceinline__ void unpack(float (&v)[4]) const {
+        v[0] = __uint_as_float(raw.x); v[1] = __uint_as_float(raw.y);
+        v[2] = __uint_as_float(raw.z); v[3] = __uint_as_float(raw.w);
     }
-    __device__ __forceinline__ void store(float* p) const {
+    static __device__ __forceinline__ void store(float* p, const float (&v)[4]) {
         st_f4(p, make_float4(v[0], v[1], v[2], v[3]));
     }
 };
 
 template <> struct Chunk<uint16_t> {
     static constexpr int N = 8;
-    float v[8];
-    __device__ __forceinline__ void load(const uint16_t* p) {
-        uint4 t = ld_nc_u4(p);
-        v[0] = bf16_lo(t.x); v[1] = bf16_hi(t.x);
-        v[2] = bf16_lo(t.y); v[3] = bf16_hi(t.y);
-        v[4] = bf16_lo(t.z); v[5] = bf16_hi(t.z);
-        v[6] = bf16_lo(t.w); v[7] = bf16_hi(t.w);
+    uint4 raw;
+    __device__ __forceinline__ void load(const uint16_t* p) { raw = ld_nc_u4(p); }
+    __device__ __forceinline__ void unpack(float (&v)[8]) const {
+        v[0] = bf16_lo(raw.x); v[1] = bf16_hi(raw.x);
+        v[2] = bf16_lo(raw.y); v[3] = bf16_hi(raw.y);
+        v[4] = bf16_lo(raw.z); v[5] = bf16_hi(raw.z);
+        v[6] = bf16_lo(raw.w); v[7] = bf16_hi(raw.w);
     }
-    __device__ __forceinline__ void store(uint16_t* p) const {
+    static __device__ __forceinline__ void store(uint16_t* p, const float (&v)[8]) {
         st_u4(p, make_uint4(bf16_pack(v[0], v[1]), bf16_pack(v[2], v[3]),
                             bf16_pack(v[4], v[5]), bf16_pack(v[6], v[7])));
     }
@@ -142,10 +148,22 @@ __device__ __forceinline__ float segment_sum(float s) {
     return s;
 }
 
-// scale = inv(sqrt(sum / width + eps)), src/backbone_cpu.jl:344, each step
-// rounded once.
-__device__ __forceinline__ float rms_scale(float sumsq, float width, float eps) {
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, width), eps)));
+// scale = inv(sqrt(sum / width + eps)), src/backbone_cpu.jl:344.  The mean
+// is a multiply by 1/width (exact for power-of-two widths, otherwise within
+// 0.5 ulp of the division) and inv(sqrt()) is one SFU rsqrt (rsqrt.approx,
+// ~2 ulp): ~3 instructions per row instead of ~30 for an IEEE division,
+// square root and second division.  The scale then differs from the
+// reference's by a few ulp (<5e-7 relative), far inside the 1e-5 bar; it
+// matters for the head kernels, where every lane recomputes it for only
+// 4-8 elements.
+__device__ __forceinline__ float rsqrt_approx(float x) {
+    float y;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float rms_scale(float sumsq, float inv_width, float eps) {
+    return rsqrt_approx(__fadd_rn(__fmul_rn(sumsq, inv_width), eps));
 }
 
 // silu(x) = x * inv(1 + exp(-x)), src/backbone.jl:196-197.  exp(-x) is
@@ -220,9 +238,9 @@ __device__ __forceinline__ const T* row_source(const RowArgs& a, int64_t row, bo
 
 // Width = 32 lanes x CHUNKS x (16 bytes / sizeof(T)); every operand 16-byte
 // aligned with 16-byte-multiple leading dimensions (checked on the host).
-template <typename T, int CHUNKS>
+// Each warp takes RPW rows per iteration and issues all their loads first.
+template <typename T, int CHUNKS, int RPW>
 __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
-    pdl_enter();
     using C = Chunk<T>;
     constexpr int N = C::N;
     constexpr int W = 32 * N * CHUNKS;
@@ -235,52 +253,65 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
 
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
-    const int64_t stride = int64_t(gridDim.x) * warps;
-    for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < a.rows;
-         row += stride) {
-        bool bad;
-        const T* xr = row_source<T>(a, row, bad);
-        C v[CHUNKS];
+    const int64_t stride = int64_t(gridDim.x) * warps * RPW;
+    for (int64_t row0 = (int64_t(blockIdx.x) * warps + (threadIdx.x >> 5)) * RPW; row0 < a.rows;
+         row0 += stride) {
+        C xv[RPW][CHUNKS], mv[RPW][CHUNKS];
+        bool bad[RPW];
 #pragma unroll
-        for (int c = 0; c < CHUNKS; ++c) v[c].load(xr + (c * 32 + lane) * N);
-        if (a.m) {
-            const T* mr = static_cast<const T*>(a.m) + row * a.ld_m;
-            C w[CHUNKS];
+        for (int k = 0; k < RPW; ++k) {
+            const int64_t row = row0 + k < a.rows ? row0 + k : a.rows - 1;
+            const T* xr = row_source<T>(a, row, bad[k]);
 #pragma unroll
-            for (int c = 0; c < CHUNKS; ++c) w[c].load(mr + (c * 32 + lane) * N);
+            for (int c = 0; c < CHUNKS; ++c) xv[k][c].load(xr + (c * 32 + lane) * N);
+            if (a.m) {
+                const T* mr = static_cast<const T*>(a.m) + row * a.ld_m;
 #pragma unroll
-            for (int c = 0; c < CHUNKS; ++c)
-#pragma unroll
-                for (int j = 0; j < N; ++j) v[c].v[j] = __fadd_rn(v[c].v[j], w[c].v[j]);
+                for (int c = 0; c < CHUNKS; ++c) mv[k][c].load(mr + (c * 32 + lane) * N);
+            }
         }
-        float s = 0.0f;
 #pragma unroll
-        for (int c = 0; c < CHUNKS; ++c)
-#pragma unroll
-            for (int j = 0; j < N; ++j) s = __fmaf_rn(v[c].v[j], v[c].v[j], s);
-        s = segment_sum<32>(s);
-        const float scale = rms_scale(s, float(W), a.eps);
-        if (bad) {
-            if (lane == 0) atomicOr(a.flag, 1);
-#pragma unroll
-            for (int c = 0; c < CHUNKS; ++c)
-#pragma unroll
-                for (int j = 0; j < N; ++j) v[c].v[j] = __int_as_float(0x7fc00000);
-        }
-        if (a.out_r) {
-            T* rr = static_cast<T*>(a.out_r) + row * a.ld_r;
-#pragma unroll
-            for (int c = 0; c < CHUNKS; ++c) v[c].store(rr + (c * 32 + lane) * N);
-        }
-        if (a.out_y) {
-            T* yr = static_cast<T*>(a.out_y) + row * a.ld_y;
+        for (int k = 0; k < RPW; ++k) {
+            const int64_t row = row0 + k;
+            if (RPW > 1 && row >= a.rows) break;
+            float v[CHUNKS][N];
+            float s = 0.0f;
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c) {
-                const float* g = gterm + (c * 32 + lane) * N;
+                xv[k][c].unpack(v[c]);
+                if (a.m) {
+                    float w[N];
+                    mv[k][c].unpack(w);
 #pragma unroll
-                for (int j = 0; j < N; ++j)
-                    v[c].v[j] = bad ? v[c].v[j] : __fmul_rn(__fmul_rn(v[c].v[j], scale), g[j]);
-                v[c].store(yr + (c * 32 + lane) * N);
+                    for (int j = 0; j < N; ++j) v[c][j] = __fadd_rn(v[c][j], w[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < N; ++j) s = __fmaf_rn(v[c][j], v[c][j], s);
+            }
+            s = segment_sum<32>(s);
+            const float scale = rms_scale(s, 1.0f / float(W), a.eps);
+            if (bad[k]) {
+                if (lane == 0) atomicOr(a.flag, 1);
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+                    for (int j = 0; j < N; ++j) v[c][j] = __int_as_float(0x7fc00000);
+            }
+            if (a.out_r) {
+                T* rr = static_cast<T*>(a.out_r) + row * a.ld_r;
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c) C::store(rr + (c * 32 + lane) * N, v[c]);
+            }
+            if (a.out_y) {
+                T* yr = static_cast<T*>(a.out_y) + row * a.ld_y;
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c) {
+                    const float* g = gterm + (c * 32 + lane) * N;
+#pragma unroll
+                    for (int j = 0; j < N; ++j)
+                        v[c][j] = bad[k] ? v[c][j] : __fmul_rn(__fmul_rn(v[c][j], scale), g[j]);
+                    C::store(yr + (c * 32 + lane) * N, v[c]);
+                }
             }
         }
     }
@@ -294,7 +325,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int64_t stride = int64_t(gridDim.x) * warps;
-    const float width = float(a.width);
+    const float inv_width = 1.0f / float(a.width);
     for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < a.rows;
          row += stride) {
         bool bad;
@@ -307,7 +338,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
             s = __fmaf_rn(r, r, s);
         }
         s = segment_sum<32>(s);
-        const float scale = rms_scale(s, width, a.eps);
+        const float scale = rms_scale(s, inv_width, a.eps);
         if (bad && lane == 0) atomicOr(a.flag, 1);
         T* rr = a.out_r ? static_cast<T*>(a.out_r) + row * a.ld_r : nullptr;
         T* yr = a.out_y ? static_cast<T*>(a.out_y) + row * a.ld_y : nullptr;
@@ -328,33 +359,69 @@ __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
 // A "unit" is one (token, head) vector of `dim` Float32 values.  LPU lanes
 // share a unit (LPU = min(32, dim/4)); 32/LPU units per warp; U units per
 // segment per iteration (their loads are all issued first).
+//
+// q/k mode can normalise two head groups in one launch -- the query heads
+// and the key heads of a token, which sit side by side in the packed
+// [q;gate | k | v] projection -- so K never pays a launch of its own.  Units
+// are token-major: unit u is head h = u mod (heads + heads2) of token
+// u / (heads + heads2); h < heads is group 1 (in, out, gamma), the rest
+// group 2 (in2, out2, gamma2).
 
 struct HeadArgs {
     float* out;
-    const float* in;     // qk: input projection; gated: o
+    float* out2;
+    const float* in;     // qk: group-1 input; gated: o
+    const float* in2;    // qk: group-2 input
     const float* z;      // gated only
     const float* gamma;
+    const float* gamma2;
     const float* cos_tab;
     const float* sin_tab;
     float eps;
-    int heads, dim, rotary;
-    int64_t units;       // tokens * heads
-    int64_t in_tok, in_head;
+    int heads, heads2, dim, rotary;
+    int64_t units;       // tokens * (heads + heads2)
+    int64_t in_tok, in_head, in2_tok, in2_head;
     int64_t z_tok, z_off;
-    int64_t out_tok;
+    int64_t out_tok, out2_tok;
     int64_t pos_offset, seq_len;
-    FastDiv heads_div;   // unit -> (token, head); units < 2^32 on the vector path
-    FastDiv seq_div;     // token -> position (divisor 1 when seq_len <= 0)
+    FastDiv heads_div;   // divisor heads + heads2; units < 2^32 on the vector path
+    FastDiv seq_div;     // token -> position (divisor = tokens when seq_len <= 0)
 };
+
+struct HeadUnit {
+    const float* src;
+    float* dst;
+    int group;  // 0 or 1
+    uint32_t tok;
+};
+
+__device__ __forceinline__ HeadUnit head_unit(const HeadArgs& a, uint32_t u, int dim) {
+    HeadUnit r;
+    const uint32_t per_tok = uint32_t(a.heads + a.heads2);
+    r.tok = fdiv(u, a.heads_div);
+    const int h = int(u - r.tok * per_tok);
+    r.group = h >= a.heads;
+    if (r.group) {
+        const int hh = h - a.heads;
+        r.src = a.in2 + int64_t(r.tok) * a.in2_tok + int64_t(hh) * a.in2_head;
+        r.dst = a.out2 + int64_t(r.tok) * a.out2_tok + int64_t(hh) * dim;
+    } else {
+        r.src = a.in + int64_t(r.tok) * a.in_tok + int64_t(h) * a.in_head;
+        r.dst = a.out + int64_t(r.tok) * a.out_tok + int64_t(h) * dim;
+    }
+    return r;
+}
 
 template <int LPU, int CHUNKS, int U, bool GATED>
 __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
     pdl_enter();
     constexpr int D = 4 * LPU * CHUNKS;
     constexpr int UPW = 32 / LPU;
-    __shared__ __align__(16) float gterm[D];
-    for (int i = threadIdx.x; i < D; i += blockDim.x)
-        gterm[i] = GATED ? a.gamma[i] : __fadd_rn(1.0f, a.gamma[i]);
+    __shared__ __align__(16) float gterm[2][D];
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        gterm[0][i] = GATED ? a.gamma[i] : __fadd_rn(1.0f, a.gamma[i]);
+        if (!GATED && a.heads2 > 0) gterm[1][i] = __fadd_rn(1.0f, a.gamma2[i]);
+    }
     __syncthreads();
 
     const int lane = threadIdx.x & 31;
@@ -365,31 +432,41 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
     const uint32_t units = uint32_t(a.units);
     const uint32_t stride = gridDim.x * warps * per_iter;
     const int half = a.rotary >> 1;
-    const int hl = half >> 2;  // lanes per rotary half
+    const int hl = half >> 2;               // lanes per rotary half
+    const bool rope_lane = !GATED && l < 2 * hl;
+    const int j = (l < hl ? l : l - hl) * 4;  // this lane's first table column
 
     for (uint32_t base = (blockIdx.x * warps + (threadIdx.x >> 5)) * per_iter; base < units;
          base += stride) {
         float4 v[U][CHUNKS];
         float4 zz[GATED ? U : 1][GATED ? CHUNKS : 1];
-        int64_t tok[U];
-        int hd[U];
+        float4 cs[GATED ? 1 : U], sn[GATED ? 1 : U];
+        HeadUnit un[U];
         bool live[U];
+        // every load of the iteration -- inputs, z, and the RoPE table rows
+        // (they depend only on the position) -- before any arithmetic
 #pragma unroll
         for (int k = 0; k < U; ++k) {
             const uint32_t u = base + uint32_t(k * UPW + seg);
             live[k] = u < units;
-            const uint32_t t = live[k] ? fdiv(u, a.heads_div) : 0u;
-            tok[k] = t;
-            hd[k] = live[k] ? int(u - t * uint32_t(a.heads)) : 0;
-            const float* src = a.in + tok[k] * a.in_tok + int64_t(hd[k]) * a.in_head;
+            un[k] = head_unit(a, live[k] ? u : 0u, D);
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c)
-                v[k][c] = live[k] ? ld_nc_f4(src + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);
+                v[k][c] = live[k] ? ld_nc_f4(un[k].src + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);
             if constexpr (GATED) {
-                const float* zs = a.z + tok[k] * a.z_tok + a.z_off + int64_t(hd[k]) * D;
+                const float* zs = a.z + int64_t(un[k].tok) * a.z_tok + a.z_off +
+                                  (un[k].src - (a.in + int64_t(un[k].tok) * a.in_tok));
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c)
                     zz[k][c] = live[k] ? ld_nc_f4(zs + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);
+            } else {
+                if (live[k] && rope_lane) {
+                    const int64_t pos = a.pos_offset + int64_t(fmod(un[k].tok, a.seq_div));
+                    cs[k] = ld_nc_f4(a.cos_tab + pos * half + j);
+                    sn[k] = ld_nc_f4(a.sin_tab + pos * half + j);
+                } else {
+                    cs[k] = sn[k] = make_float4(0, 0, 0, 0);
+                }
             }
         }
 #pragma unroll
@@ -403,10 +480,11 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
                 s = __fmaf_rn(v[k][c].w, v[k][c].w, s);
             }
             s = segment_sum<LPU>(s);
-            const float scale = rms_scale(s, float(D), a.eps);
+            const float scale = rms_scale(s, 1.0f / float(D), a.eps);
+            const float* gt = gterm[GATED ? 0 : un[k].group];
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c) {
-                const float4 g = *reinterpret_cast<const float4*>(gterm + (c * LPU + l) * 4);
+                const float4 g = *reinterpret_cast<const float4*>(gt + (c * LPU + l) * 4);
                 float4& x = v[k][c];
                 x.x = __fmul_rn(__fmul_rn(x.x, scale), g.x);
                 x.y = __fmul_rn(__fmul_rn(x.y, scale), g.y);
@@ -430,31 +508,26 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
                     p.y = __shfl_sync(kFull, v[k][0].y, partner);
                     p.z = __shfl_sync(kFull, v[k][0].z, partner);
                     p.w = __shfl_sync(kFull, v[k][0].w, partner);
-                    if (live[k] && l < 2 * hl) {
-                        const int64_t pos =
-                            a.pos_offset + int64_t(fmod(uint32_t(tok[k]), a.seq_div));
-                        const int j = (l < hl ? l : l - hl) * 4;
-                        const float4 cs = ld_nc_f4(a.cos_tab + pos * half + j);
-                        const float4 sn = ld_nc_f4(a.sin_tab + pos * half + j);
+                    if (live[k] && rope_lane) {
                         float4& x = v[k][0];
+                        const float4 c4 = cs[k], s4 = sn[k];
                         if (l < hl) {  // a*cos - b*sin
-                            x.x = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(p.x, sn.x));
-                            x.y = __fsub_rn(__fmul_rn(x.y, cs.y), __fmul_rn(p.y, sn.y));
-                            x.z = __fsub_rn(__fmul_rn(x.z, cs.z), __fmul_rn(p.z, sn.z));
-                            x.w = __fsub_rn(__fmul_rn(x.w, cs.w), __fmul_rn(p.w, sn.w));
+                            x.x = __fsub_rn(__fmul_rn(x.x, c4.x), __fmul_rn(p.x, s4.x));
+                            x.y = __fsub_rn(__fmul_rn(x.y, c4.y), __fmul_rn(p.y, s4.y));
+                            x.z = __fsub_rn(__fmul_rn(x.z, c4.z), __fmul_rn(p.z, s4.z));
+                            x.w = __fsub_rn(__fmul_rn(x.w, c4.w), __fmul_rn(p.w, s4.w));
                         } else {       // b*cos + a*sin
-                            x.x = __fadd_rn(__fmul_rn(x.x, cs.x), __fmul_rn(p.x, sn.x));
-                            x.y = __fadd_rn(__fmul_rn(x.y, cs.y), __fmul_rn(p.y, sn.y));
-                            x.z = __fadd_rn(__fmul_rn(x.z, cs.z), __fmul_rn(p.z, sn.z));
-                            x.w = __fadd_rn(__fmul_rn(x.w, cs.w), __fmul_rn(p.w, sn.w));
+                            x.x = __fadd_rn(__fmul_rn(x.x, c4.x), __fmul_rn(p.x, s4.x));
+                            x.y = __fadd_rn(__fmul_rn(x.y, c4.y), __fmul_rn(p.y, s4.y));
+                            x.z = __fadd_rn(__fmul_rn(x.z, c4.z), __fmul_rn(p.z, s4.z));
+                            x.w = __fadd_rn(__fmul_rn(x.w, c4.w), __fmul_rn(p.w, s4.w));
                         }
                     }
                 }
             }
             if (live[k]) {
-                float* dst = a.out + tok[k] * a.out_tok + int64_t(hd[k]) * D;
 #pragma unroll
-                for (int c = 0; c < CHUNKS; ++c) st_f4(dst + (c * LPU + l) * 4, v[k][c]);
+                for (int c = 0; c < CHUNKS; ++c) st_f4(un[k].dst + (c * LPU + l) * 4, v[k][c]);
             }
         }
     }
@@ -469,37 +542,42 @@ __global__ void __launch_bounds__(kThreads) head_norm_generic(HeadArgs a) {
     const int warps = blockDim.x >> 5;
     const int64_t stride = int64_t(gridDim.x) * warps;
     const int half = a.rotary >> 1;
+    const int64_t per_tok = a.heads + a.heads2;
     for (int64_t u = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); u < a.units; u += stride) {
-        const int64_t tok = u / a.heads;
-        const int hd = int(u - tok * a.heads);
-        const float* src = a.in + tok * a.in_tok + int64_t(hd) * a.in_head;
+        const int64_t tok = u / per_tok;
+        const int h = int(u - tok * per_tok);
+        const bool second = h >= a.heads;
+        const int hh = second ? h - a.heads : h;
+        const float* src = second ? a.in2 + tok * a.in2_tok + int64_t(hh) * a.in2_head
+                                  : a.in + tok * a.in_tok + int64_t(hh) * a.in_head;
+        float* dst = second ? a.out2 + tok * a.out2_tok + int64_t(hh) * a.dim
+                            : a.out + tok * a.out_tok + int64_t(hh) * a.dim;
+        const float* gamma = second ? a.gamma2 : a.gamma;
         float s = 0.0f;
         for (int i = lane; i < a.dim; i += 32) {
             const float x = __ldg(src + i);
             s = __fmaf_rn(x, x, s);
         }
         s = segment_sum<32>(s);
-        const float scale = rms_scale(s, float(a.dim), a.eps);
-        float* dst = a.out + tok * a.out_tok + int64_t(hd) * a.dim;
+        const float scale = rms_scale(s, 1.0f / float(a.dim), a.eps);
         if constexpr (GATED) {
-            const float* zs = a.z + tok * a.z_tok + a.z_off + int64_t(hd) * a.dim;
+            const float* zs = a.z + tok * a.z_tok + a.z_off + int64_t(hh) * a.dim;
             for (int i = lane; i < a.dim; i += 32) {
-                const float y = __fmul_rn(__fmul_rn(__ldg(src + i), scale), a.gamma[i]);
+                const float y = __fmul_rn(__fmul_rn(__ldg(src + i), scale), gamma[i]);
                 dst[i] = __fmul_rn(y, silu(__ldg(zs + i)));
             }
         } else {
             const int64_t pos = a.pos_offset + (a.seq_len > 0 ? tok % a.seq_len : tok);
             for (int i = lane; i < a.dim; i += 32) {
-                const float y = __fmul_rn(__fmul_rn(__ldg(src + i), scale),
-                                          __fadd_rn(1.0f, a.gamma[i]));
+                const float y = __fmul_rn(__fmul_rn(__ldg(src + i), scale), __fadd_rn(1.0f, gamma[i]));
                 float out = y;
                 if (i < 2 * half) {
-                    const int j = i < half ? i : i - half;
+                    const int jj = i < half ? i : i - half;
                     const int q = i < half ? i + half : i - half;
                     const float p = __fmul_rn(__fmul_rn(__ldg(src + q), scale),
-                                              __fadd_rn(1.0f, a.gamma[q]));
-                    const float c = __ldg(a.cos_tab + pos * half + j);
-                    const float sn = __ldg(a.sin_tab + pos * half + j);
+                                              __fadd_rn(1.0f, gamma[q]));
+                    const float c = __ldg(a.cos_tab + pos * half + jj);
+                    const float sn = __ldg(a.sin_tab + pos * half + jj);
                     out = i < half ? __fsub_rn(__fmul_rn(y, c), __fmul_rn(p, sn))
                                    : __fadd_rn(__fmul_rn(y, c), __fmul_rn(p, sn));
                 }

@@ -66,6 +66,8 @@ SIGNATURES = {
                          _i64, _int, _vp],
     "qdc_qk_norm_rope": [_vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _vp, _flt, _int, _vp, _vp,
                          _i64, _i64, _i64, _vp],
+    "qdc_q_k_norm_rope": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _i64, _i64,
+                          _vp, _vp, _flt, _int, _vp, _vp, _i64, _i64, _i64, _vp],
     "qdc_gated_rms": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],
 }

@@ -1,0 +1,292 @@
+"""QwenBackbone on B200: the reference's forward with every per-layer row op
+on libqdc_b200's sm_100a kernels.
+
+Public API, mirroring src/backbone.jl:
+  QwenBackbone.from_directory(dir, device)   QwenBackbone(dir; device), :74-192
+  backbone_hidden(b, ids, mask[, positions])  :433-460 (host float32 (tokens, hidden))
+  backbone_last_hidden(b, ids, mask)          :470-490
+  batch_hidden(b, ids, mask)                  many equal-length sequences in one
+                                              pass (the batched forward the
+                                              reference leaves to accelerators,
+                                              :66-70); device (B*S, hidden)
+
+Per layer (native_layer, src/backbone.jl:363-382):
+  input norm   -- qdc gather+norm for layer 0, else fused into the previous
+                  layer's MLP residual add (qdc_residual_rms)
+  attention    -- full: one [q;k;v] GEMM, qdc q/k norm + partial RoPE,
+                  causal GQA attention (torch SDPA), sigmoid gate, o GEMM;
+                  delta: one [qkv;z;a;b] GEMM, causal 4-tap conv + SiLU, q/k
+                  L2 norms, gates, chunked gated delta rule (torch), qdc gated
+                  norm reading z in place, out GEMM
+  post norm    -- qdc residual add + RMSNorm
+  MLP          -- one [gate;up] GEMM, qdc SwiGLU, down GEMM
+  residual add -- fused with the next layer's input norm / the final norm.
+
+The projections, attention, conv and delta rule are the reference's
+out-of-scope parts; they run as plain torch Float32 ops (cuBLAS GEMMs with
+TF32 disabled, as the reference computes in Float32, src/backbone.jl:14-16).
+"""
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from ._lib import ArgumentError
+from .model import Config, load_weights, pack_layers, random_weights
+
+FLOATMAX32 = float(np.finfo(np.float32).max)
+DELTA_CHUNK = 64  # src/backbone.jl:301, ext/cuda_delta_chunked.jl:9
+
+
+def _device_f32(x, device):
+    t = x if torch.is_tensor(x) else torch.from_numpy(np.ascontiguousarray(x, np.float32))
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+def check_sequence(vocab, ids, mask):
+    """src/backbone.jl:413-422."""
+    if len(ids) != len(mask):
+        raise ArgumentError(1, "Input IDs and mask must have identical lengths.")
+    if len(ids) == 0:
+        raise ArgumentError(1, "Inputs must not be empty.")
+    ids_a = np.asarray(ids)
+    if ids_a.min() < 0 or ids_a.max() >= vocab:
+        raise ArgumentError(2, "Token ID is outside the vocabulary.")
+    m = np.asarray(mask)
+    if not np.isin(m, (0, 1)).all():
+        raise ArgumentError(1, "Mask values must be zero or one.")
+
+
+class QwenBackbone:
+    def __init__(self, config, weights, device="cuda"):
+        self.config = config
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ArgumentError(1, "QwenBackbone(…; device) needs a CUDA device: the per-layer "
+                                   "kernels have no CPU path")
+        self.ctx = ops.context(self.device)
+        self.embedding = _device_f32(weights["embed_tokens.weight"], self.device)
+        self.final_norm = _device_f32(weights["norm.weight"], self.device)
+        self.layers = pack_layers(config, weights, self.device)
+        self._rope = {}
+        self.trace = None  # list to record (site, inputs, outputs) of every qdc call
+
+    @classmethod
+    def from_directory(cls, directory, device="cuda"):
+        config, weights = load_weights(directory)
+        return cls(config, weights, device)
+
+    @classmethod
+    def random(cls, config, seed=0, device="cuda"):
+        return cls(config, random_weights(config, seed, device=device), device)
+
+    # ------------------------------------------------------------ helpers
+
+    def rope(self, n):
+        """Device cos/sin tables for positions 0..n-1 (src/backbone_cpu.jl:90-105)."""
+        rows = max(int(n), 1)
+        hit = self._rope.get(self.config.rotary_dim)
+        if hit is None or hit[0].shape[0] < rows:
+            hit = ops.rope_table(self.config.rope_theta, self.config.rotary_dim, rows,
+                                 device=self.device)
+            self._rope[self.config.rotary_dim] = hit
+        return hit
+
+    def _record(self, site, inputs, outputs):
+        if self.trace is not None:
+            clone = lambda t: None if t is None else t.detach().clone()
+            self.trace.append((site, tuple(clone(t) for t in inputs),
+                               tuple(clone(t) for t in outputs)))
+
+    # ------------------------------------------------------ attention parts
+
+    def _full_attention(self, layer, y, mask, B, S):
+        cfg = self.config
+        D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+        T = B * S
+        proj = y @ layer["qkv"].t()
+        qw, kw = Hq * 2 * D, Hkv * D
+        qgate = proj[:, :qw].view(T, Hq, 2 * D)
+        k_raw = proj[:, qw:qw + kw].view(T, Hkv, D)
+        v = proj[:, qw + kw:].view(T, Hkv, D)
+        cos, sin = self.rope(S)
+        q, k = ops.native_q_k_norm_rope(qgate[:, :, :D], k_raw, layer["q_norm"], layer["k_norm"],
+                                        cfg.eps, cfg.rotary_dim, cos, sin, seq_len=S, ctx=self.ctx)
+        self._record("q_norm_rope", (qgate[:, :, :D],), (q,))
+        self._record("k_norm_rope", (k_raw,), (k,))
+        qh = q.view(B, S, Hq, D).transpose(1, 2)
+        kh = k.view(B, S, Hkv, D).transpose(1, 2)
+        vh = v.reshape(B, S, Hkv, D).transpose(1, 2)
+        # key i visible to query j iff i <= j and mask[i] == 1, else -floatmax
+        # (src/backbone.jl:237-242): a fully hidden query averages every key.
+        if bool((mask == 1).all()):
+            out = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
+        else:
+            causal = torch.ones((S, S), dtype=torch.bool, device=self.device).tril()
+            allowed = causal[None] & (mask.view(B, 1, S) == 1)
+            bias = torch.zeros((B, 1, S, S), dtype=torch.float32, device=self.device)
+            bias.masked_fill_(~allowed[:, None], -FLOATMAX32)
+            out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=bias, enable_gqa=True)
+        gate = torch.sigmoid(qgate[:, :, D:])
+        out = out.transpose(1, 2).reshape(T, Hq, D) * gate
+        return out.reshape(T, Hq * D) @ layer["out"].t()
+
+    def _delta_attention(self, layer, y, mask, B, S):
+        cfg = self.config
+        T = B * S
+        kw, vw, C = cfg.key_width, cfg.value_width, cfg.qkv_width
+        masked = y * mask.view(T, 1).to(torch.float32)
+        proj = masked @ layer["proj"].t()  # [qkv | z | a | b] per token
+        qkv = proj[:, :C].view(B, S, C)
+        # causal depthwise conv, taps accumulated oldest first (src/backbone_cpu.jl:787-807)
+        Kt = layer["conv"].shape[1]
+        padded = F.pad(qkv, (0, 0, Kt - 1, 0))
+        acc = padded[:, 0:S] * layer["conv"][:, 0]
+        for j in range(1, Kt):
+            acc = acc + padded[:, j:j + S] * layer["conv"][:, j]
+        mixed = acc * torch.sigmoid(acc)
+        q = mixed[..., :kw].reshape(B, S, cfg.key_heads, cfg.key_dim)
+        k = mixed[..., kw:2 * kw].reshape(B, S, cfg.key_heads, cfg.key_dim)
+        v = mixed[..., 2 * kw:].reshape(B, S, cfg.value_heads, cfg.value_dim)
+        q = q / (torch.sqrt((q * q).sum(-1, keepdim=True) + 1e-6) * math.sqrt(cfg.key_dim))
+        k = k / torch.sqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+        a = proj[:, C + vw:C + vw + cfg.value_heads].view(B, S, cfg.value_heads)
+        b = proj[:, C + vw + cfg.value_heads:C + vw + 2 * cfg.value_heads].view(B, S, cfg.value_heads)
+        beta = torch.sigmoid(b)
+        decay = layer["a_decay"] * F.softplus(a + layer["dt_bias"])
+        o = chunked_delta(q, k, v, beta, decay, cfg.value_heads // cfg.key_heads)
+        o = o.reshape(T, cfg.value_heads, cfg.value_dim)
+        z = proj[:, C:C + vw].view(T, cfg.value_heads, cfg.value_dim)
+        gated = ops.native_gated_rms(o, z, layer["norm"], cfg.eps, ctx=self.ctx)
+        self._record("gated_rms", (o, z), (gated,))
+        return gated @ layer["out"].t()
+
+    # -------------------------------------------------------------- forward
+
+    def _forward(self, ids, mask, B, S):
+        """Final-normalized states (B*S, hidden) on the device.  ids: host
+        int array (B*S,), mask: device int tensor (B*S,)."""
+        cfg = self.config
+        prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            layers = self.layers
+            x, y = ops.native_gather_rms(self.embedding, ids, layers[0]["input_norm"], cfg.eps,
+                                         ctx=self.ctx)
+            self._record("gather_rms", (), (x, y))
+            for i, layer in enumerate(layers):
+                if layer["kind"] == "full":
+                    mixed = self._full_attention(layer, y, mask, B, S)
+                else:
+                    mixed = self._delta_attention(layer, y, mask, B, S)
+                r, y = ops.native_residual_rms(x, mixed, layer["post_norm"], cfg.eps, ctx=self.ctx)
+                self._record("post_rms", (x, mixed), (r, y))
+                gu = y @ layer["gate_up"].t()
+                I = cfg.intermediate
+                h, _ = ops.native_mlp_gate(gu[:, :I], gu[:, I:], ctx=self.ctx)
+                self._record("swiglu", (gu[:, :I], gu[:, I:]), (h,))
+                mlp = h @ layer["down"].t()
+                nxt = layers[i + 1]["input_norm"] if i + 1 < len(layers) else self.final_norm
+                r_in = r.clone() if self.trace is not None else None
+                x, y = ops.native_residual_add_rms(r, mlp, nxt, cfg.eps, ctx=self.ctx)
+                self._record("mlp_rms" if i + 1 < len(layers) else "final_rms", (r_in, mlp), (x, y))
+            return y
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+
+    def batch_hidden(self, ids, mask=None):
+        """Final-normalized states of B equal-length sequences, (B*S, hidden)
+        on the device.  ids / mask: (B, S) host arrays (mask default ones)."""
+        ids = np.asarray(ids)
+        if ids.ndim != 2:
+            raise ArgumentError(1, "batch_hidden takes (batch, sequence) ids")
+        B, S = ids.shape
+        mask = np.ones_like(ids) if mask is None else np.asarray(mask)
+        if mask.shape != ids.shape:
+            raise ArgumentError(1, "Input IDs and mask must have identical lengths.")
+        check_sequence(self.config.vocab, ids.reshape(-1), mask.reshape(-1))
+        dmask = torch.from_numpy(mask.reshape(-1).astype(np.int32)).to(self.device)
+        with self.ctx.lock:
+            y = self._forward(ids.reshape(-1).astype(np.int32), dmask, B, S)
+            self.ctx.sync()
+        return y
+
+
+def backbone_hidden(backbone, ids, mask, positions=None):
+    """src/backbone.jl:433-460: one sequence, returns host float32 (tokens,
+    hidden) final-normalized states (all positions, or `positions`, 1-based
+    as in the reference)."""
+    ids = np.asarray(ids).reshape(-1) if np.ndim(ids) == 1 else np.asarray(ids)
+    mask = np.asarray(mask)
+    if ids.ndim == 2:
+        if ids.shape[0] != 1 or mask.shape[0] != 1:
+            raise ArgumentError(1, "Pass one sequence per call; batching is not implemented yet.")
+        ids, mask = ids.reshape(-1), mask.reshape(-1)
+    check_sequence(backbone.config.vocab, ids, mask)
+    states = backbone.batch_hidden(ids.reshape(1, -1), mask.reshape(1, -1)).cpu().numpy()
+    if positions is None:
+        return states
+    pos = np.asarray(positions)
+    if pos.size and (pos.min() < 1 or pos.max() > states.shape[0]):
+        raise ArgumentError(1, "Position is outside the sequence.")
+    return states[pos - 1]
+
+
+def backbone_last_hidden(backbone, ids, mask):
+    """src/backbone.jl:470-490: the last position's state, host vector."""
+    check_sequence(backbone.config.vocab, np.asarray(ids).reshape(-1), np.asarray(mask).reshape(-1))
+    return backbone_hidden(backbone, ids, mask)[-1]
+
+
+def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK):
+    """Gated delta rule in 64-token chunks (src/backbone.jl:309-343), batched
+    over sequences, value heads and chunks; only the state hand-off between
+    chunks is sequential.
+
+    q, k: (B, S, Hk, Dk) normalised; v: (B, S, Hv, Dv); beta, decay: (B, S, Hv).
+    Returns o: (B, S, Hv, Dv).  A short last chunk is zero-padded: padded
+    tokens have beta = 0, k = q = v = 0 and decay 0, so they change neither
+    the real tokens' outputs nor the carried state."""
+    B, S, Hk, Dk = q.shape
+    Hv, Dv = v.shape[2], v.shape[3]
+    n = (S + chunk - 1) // chunk
+    P = n * chunk - S
+    idx = torch.arange(Hv, device=q.device) // groups  # kv head of value head h: cld(h, groups)
+
+    def per_head(t, heads_idx=None):  # (B, S, H, D) -> (B, H, n, C, D)
+        if heads_idx is not None:
+            t = t[:, :, heads_idx]
+        t = F.pad(t, (0, 0, 0, 0, 0, P))
+        return t.view(B, n, chunk, t.shape[2], t.shape[3]).permute(0, 3, 1, 2, 4)
+
+    Q, K, V = per_head(q, idx), per_head(k, idx), per_head(v)
+    bet = F.pad(beta, (0, 0, 0, P)).view(B, n, chunk, Hv).permute(0, 3, 1, 2)   # (B,H,n,C)
+    g = F.pad(decay, (0, 0, 0, P)).view(B, n, chunk, Hv).permute(0, 3, 1, 2)
+    cum = torch.cumsum(g, dim=-1)
+    lower = torch.ones((chunk, chunk), dtype=torch.bool, device=q.device).tril()
+    diff = cum[..., :, None] - cum[..., None, :]
+    pair = torch.where(lower, torch.exp(torch.where(lower, diff, torch.zeros_like(diff))),
+                       torch.zeros_like(diff))                                 # (B,H,n,C,C)
+    kb = K * bet[..., None]
+    system = (kb @ K.transpose(-1, -2)) * pair
+    L = torch.tril(system, diagonal=-1) + torch.eye(chunk, device=q.device)
+    e = torch.exp(cum)[..., None]
+    new_values = torch.linalg.solve_triangular(L, V * bet[..., None], upper=False, unitriangular=True)
+    reading = torch.linalg.solve_triangular(L, kb * e, upper=False, unitriangular=True)
+    intra_t = (Q @ K.transpose(-1, -2)) * pair                                  # [j, i] = q_j k_i pair[j,i]
+    qe = Q * e
+    end = cum[..., -1:]
+    ending = K * torch.exp(end - cum)[..., None]
+    final = torch.exp(end)[..., None]                                           # (B,H,n,1,1)
+    state = torch.zeros((B, Hv, Dv, Dk), dtype=q.dtype, device=q.device)
+    # token-major output, heads contiguous within a token (the layout the
+    # gated norm reads)
+    out = torch.empty((B, n, chunk, Hv, Dv), dtype=q.dtype, device=q.device)
+    for c in range(n):
+        corr = new_values[:, :, c] - reading[:, :, c] @ state.transpose(-1, -2)  # (B,H,C,Dv)
+        out[:, c] = (qe[:, :, c] @ state.transpose(-1, -2) + intra_t[:, :, c] @ corr).transpose(1, 2)
+        state = state * final[:, :, c] + corr.transpose(-1, -2) @ ending[:, :, c]
+    out = out.view(B, n * chunk, Hv, Dv)
+    return out if P == 0 else out[:, :S].contiguous()

@@ -11,6 +11,7 @@ for CuArrays and the work done by the library's sm_100a kernels:
                        fused with the next native_rms
   native_qk_norm_rope  native_rms + native_rope of full_attention,
                        src/backbone.jl:206-235 (CPU form src/backbone_cpu.jl:113-136)
+  native_q_k_norm_rope the same for the query and key heads in one launch
   native_gated_rms     src/backbone.jl:339-341, ext/cuda_delta.jl:99-116
   native_mlp_gate      src/backbone.jl:352-355, ext/cuda_mlp.jl:49-61
   rope_table           src/backbone_cpu.jl:90-105
@@ -346,6 +347,53 @@ def native_qk_norm_rope(x, weight, eps, rotary, cos, sin, *, pos_offset=0, seq_l
             float(eps), int(rotary), _ptr(cos) if rotary else None, _ptr(sin) if rotary else None,
             rows, int(pos_offset), int(seq_len or 0), _stream(dev, stream)), ctx.handle)
     return out
+
+
+def native_q_k_norm_rope(q_in, k_in, q_weight, k_weight, eps, rotary, cos, sin, *, pos_offset=0,
+                        seq_len=None, q_out=None, k_out=None, ctx=None, stream=None):
+    """The query and key halves of native_qk_norm_rope in ONE launch:
+    q_in (tokens, q_heads, dim), k_in (tokens, k_heads, dim) views (e.g. both
+    slices of the packed [q;gate | k | v] projection).  Returns dense
+    (q, k)."""
+    dev = _cuda(q_in, k_in, q_weight, k_weight, cos, sin, q_out, k_out)
+    for x, name in ((q_in, "q"), (k_in, "k")):
+        if x.dim() != 3 or (x.numel() and x.shape[2] > 1 and x.stride(2) != 1):
+            raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} must be (tokens, heads, dim) with unit "
+                                                     "inner stride")
+        if x.dtype != torch.float32:
+            raise ArgumentError(_lib.QDC_EINVAL, "q/k norm takes Float32 projections")
+    tokens, qh, dim = q_in.shape
+    if k_in.shape[0] != tokens or k_in.shape[2] != dim:
+        raise DimensionMismatch(_lib.QDC_EINVAL, "q and k shapes differ")
+    kh = k_in.shape[1]
+    q_weight, k_weight = _gamma(q_weight, dim, dev), _gamma(k_weight, dim, dev)
+    if rotary % 2 or rotary > dim or rotary < 0:
+        raise ArgumentError(_lib.QDC_EINVAL, "rotary dims must be even and <= head_dim")
+    rows = 0
+    if rotary > 0:
+        if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] != rotary // 2:
+            raise DimensionMismatch(_lib.QDC_EINVAL, "RoPE table shape differs")
+        cos, sin = cos.contiguous(), sin.contiguous()
+        rows = cos.shape[0]
+    if q_out is None:
+        q_out = torch.empty((tokens, qh, dim), dtype=torch.float32, device=dev)
+    if k_out is None:
+        k_out = torch.empty((tokens, kh, dim), dtype=torch.float32, device=dev)
+    for t, shape in ((q_out, (tokens, qh, dim)), (k_out, (tokens, kh, dim))):
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise DimensionMismatch(_lib.QDC_EINVAL, "output shape differs")
+    strides = []
+    for x, heads in ((q_in, qh), (k_in, kh)):
+        strides.append(x.stride(0) if tokens > 1 else heads * dim)
+        strides.append(x.stride(1) if heads > 1 else dim)
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_q_k_norm_rope(
+            ctx.handle, _ptr(q_out), _ptr(k_out), _ptr(q_in), _ptr(k_in), tokens, qh, kh, dim,
+            strides[0], strides[1], strides[2], strides[3], _ptr(q_weight), _ptr(k_weight),
+            float(eps), int(rotary), _ptr(cos) if rotary else None, _ptr(sin) if rotary else None,
+            rows, int(pos_offset), int(seq_len or 0), _stream(dev, stream)), ctx.handle)
+    return q_out, k_out
 
 
 def native_gated_rms(o, z, weight, eps, *, out=None, ctx=None, stream=None):

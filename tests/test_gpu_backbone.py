@@ -1,0 +1,180 @@
+"""The whole forward on the B200 (qdc kernels at every per-layer site,
+out-of-scope parts in torch Float32) against the reference's golden logits
+and the CPU oracle forward.
+
+Mirrors the reference's hardware suite (test/cuda.jl:7-31: GPU vs CPU on the
+fixture and a synthetic hybrid backbone, lengths 1..257, masks with holes
+every third token, atol = rtol = 2e-5) and its fixture test
+(test/backbone.jl:1-34).  The site-level test replays every per-layer kernel
+call of a BASELINE config-1 forward through the oracle and checks it at the
+kernel bar (1e-6 + 1e-5 |b|)."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+
+@pytest.fixture(scope="module")
+def q():
+    import qdc_b200
+    return qdc_b200
+
+
+@pytest.fixture(scope="module")
+def fixture_model(q):
+    return q.QwenBackbone.from_directory(GOLDEN, device="cuda")
+
+
+@pytest.fixture(scope="module")
+def readout():
+    from oracle import forward as F
+    return F.read_safetensors(os.path.join(GOLDEN, "readout.safetensors"))["weight"].astype(np.float64)
+
+
+def _violation(actual, expected):
+    return float((np.abs(actual - expected) / (TOL + TOL * np.abs(expected))).max())
+
+
+@pytest.mark.parametrize("name", ["reference.json", "cuda_reference.json"])
+def test_fixture_logits(q, fixture_model, readout, name):
+    with open(os.path.join(GOLDEN, name)) as f:
+        samples = json.load(f)
+    worst = 0.0
+    for s in samples:
+        expected = np.array(s["logits"], np.float64)
+        ids_rows, mask_rows = s["inputs"]["input_ids"], s["inputs"]["attention_mask"]
+        actual = np.array([readout @ q.backbone_hidden(fixture_model, ids, mask)[-1]
+                           for ids, mask in zip(ids_rows, mask_rows)])
+        worst = max(worst, _violation(actual, expected))
+        for ids, mask in zip(ids_rows, mask_rows):
+            last = q.backbone_last_hidden(fixture_model, ids, mask)
+            assert _violation(last.astype(np.float64),
+                              q.backbone_hidden(fixture_model, ids, mask)[-1]) <= 1.0
+    assert worst <= 1.0
+
+
+def test_fixture_validation(q, fixture_model):
+    # test/backbone.jl:27-33
+    for ids, mask in (([1, 2], [1]), ([], []), ([1, 2], [1, 2]), ([64], [1])):
+        with pytest.raises(q.ArgumentError):
+            q.backbone_hidden(fixture_model, ids, mask)
+    with pytest.raises(q.ArgumentError):
+        q.backbone_hidden(fixture_model, [1, 2, 3], [1, 1, 1], positions=[0])
+
+
+def config1():
+    """vocab 4096, hidden 256, [GDN, GDN, GDN, full], 4 q /
+    2 kv heads x 64, rotary 16 of 64, theta 1e7, eps 1e-6, intermediate 768;
+    DeltaNet heads of the reference's synthetic backbone (benchmark/synthetic.jl:4-6:
+    key 2 x 128, value 4 x 128)."""
+    from qdc_b200.model import Config
+    return Config(hidden=256, head_dim=64, heads=4, kv_heads=2, key_heads=2, value_heads=4,
+                  key_dim=128, value_dim=128, eps=float(np.float32(1e-6)),
+                  rope_theta=float(np.float32(1e7)), rotary_dim=16, vocab=4096, intermediate=768,
+                  layer_types=["linear_attention"] * 3 + ["full_attention"])
+
+
+@pytest.fixture(scope="module")
+def cfg1_pair(q):
+    from oracle import forward as F
+    cfg = config1()
+    model = q.QwenBackbone.random(cfg, seed=7, device="cuda")
+    from qdc_b200.model import random_weights
+    weights = {k: v.cpu().numpy() for k, v in random_weights(cfg, 7, device="cuda").items()}
+    ocfg = F.Config(**{k: getattr(cfg, k) for k in F.Config.__dataclass_fields__})
+    return model, F.Model(ocfg, weights)
+
+
+@pytest.mark.parametrize("n", [1, 9, 63, 64, 65, 129])
+@pytest.mark.parametrize("holes", [False, True])
+def test_config1_forward_matches_oracle(q, cfg1_pair, n, holes):
+    from oracle import forward as F
+    model, omodel = cfg1_pair
+    rng = np.random.default_rng(n)
+    ids = rng.integers(0, 4096, n)
+    mask = np.ones(n, np.int64)
+    if holes and n > 1:
+        mask[0:n - 1:3] = 0  # test/cuda.jl:13
+    expected = F.backbone_hidden(omodel, ids, mask)
+    actual = q.backbone_hidden(model, ids, mask)
+    assert actual.shape == (n, 256)
+    assert _violation(actual.astype(np.float64), expected.astype(np.float64)) <= 1.0
+
+
+def test_config1_batch_two_by_64(q, cfg1_pair):
+    """BASELINE config 1's batch: 2 x 64, full mask, both rows in one pass."""
+    from oracle import forward as F
+    model, omodel = cfg1_pair
+    rng = np.random.default_rng(0)
+    ids = rng.integers(0, 4096, (2, 64))
+    out = model.batch_hidden(ids).cpu().numpy().reshape(2, 64, 256)
+    for b in range(2):
+        expected = F.backbone_hidden(omodel, ids[b], np.ones(64, np.int64))
+        assert _violation(out[b].astype(np.float64), expected.astype(np.float64)) <= 1.0
+
+
+def test_config1_every_kernel_site(q, cfg1_pair, oracle):
+    """Every per-layer kernel call of a config-1 forward, replayed through
+    the oracle on the same inputs, within 1e-6 + 1e-5 |b|."""
+    model, omodel = cfg1_pair
+    cfg = model.config
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, 4096, (2, 64))
+    model.trace = []
+    try:
+        model.batch_hidden(ids)
+        trace = model.trace
+    finally:
+        model.trace = None
+    n_layers = len(cfg.layer_types)
+    kinds = [site for site, _, _ in trace]
+    assert kinds.count("gather_rms") == 1 and kinds.count("post_rms") == n_layers
+    assert kinds.count("swiglu") == n_layers and kinds.count("gated_rms") == 3
+    assert kinds.count("q_norm_rope") == 1 and kinds.count("k_norm_rope") == 1
+    assert kinds.count("mlp_rms") == n_layers - 1 and kinds.count("final_rms") == 1
+    w = omodel.weights
+    cos, sin = oracle.rope_table(cfg.rope_theta, cfg.rotary_dim, 64)
+    layer = 0
+
+    def cpu(t):
+        return t.cpu().numpy()
+
+    def close(a, e):
+        a, e = np.asarray(a, np.float64), np.asarray(e, np.float64)
+        return bool((np.abs(a - e) <= 1e-6 + 1e-5 * np.abs(e)).all())
+
+    for site, ins, outs in trace:
+        p = f"layers.{layer}."
+        if site == "gather_rms":
+            ex_x, ex_y = oracle.gather_rms(w["embed_tokens.weight"], ids.reshape(-1), None,
+                                           w["layers.0.input_layernorm.weight"], cfg.eps)
+            assert np.array_equal(cpu(outs[0]), ex_x) and close(cpu(outs[1]), ex_y)
+        elif site in ("q_norm_rope", "k_norm_rope"):
+            x = cpu(ins[0])
+            gam = w[p + ("self_attn.q_norm.weight" if site[0] == "q" else "self_attn.k_norm.weight")]
+            ex = oracle.qk_norm_rope(np.ascontiguousarray(x), gam, cfg.eps, cfg.rotary_dim, cos, sin,
+                                     seq_len=64)
+            assert close(cpu(outs[0]), ex), site
+        elif site == "gated_rms":
+            o, z = cpu(ins[0]), np.ascontiguousarray(cpu(ins[1]))
+            ex = oracle.gated_rms(o, z, w[p + "linear_attn.norm.weight"], cfg.eps)
+            assert close(cpu(outs[0]), ex), site
+        elif site == "post_rms":
+            ex_r, ex_y = oracle.residual_rms(cpu(ins[0]), cpu(ins[1]),
+                                             w[p + "post_attention_layernorm.weight"], cfg.eps)
+            assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), site
+        elif site == "swiglu":
+            ex, _ = oracle.swiglu(np.ascontiguousarray(cpu(ins[0])), np.ascontiguousarray(cpu(ins[1])))
+            assert close(cpu(outs[0]), ex), site
+        elif site in ("mlp_rms", "final_rms"):
+            gam = w[f"layers.{layer + 1}.input_layernorm.weight"] if site == "mlp_rms" else w["norm.weight"]
+            ex_r, ex_y = oracle.residual_rms(cpu(ins[0]), cpu(ins[1]), gam, cfg.eps)
+            assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), site
+            layer += 1

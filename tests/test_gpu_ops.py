@@ -316,3 +316,29 @@ def test_workspace_arena(q):
     a.fill_(1.0)
     torch.cuda.synchronize()
     ctx.close()
+
+
+@pytest.mark.parametrize("tokens,qh,kh,dim,rotary", [(33, 8, 2, 256, 64), (17, 4, 2, 64, 16),
+                                                     (9, 2, 1, 4, 4), (1, 8, 2, 256, 64),
+                                                     (65, 3, 1, 128, 128), (5, 2, 2, 96, 32)])
+def test_q_k_norm_rope_one_launch(q, oracle, tokens, qh, kh, dim, rotary):
+    """Query and key heads of the packed [q;gate | k | v] projection in one
+    launch, each against the oracle."""
+    r = rng(tokens + qh + dim)
+    width = qh * 2 * dim + 2 * kh * dim
+    proj = r.normal(0, 1, (tokens, width)).astype(np.float32)
+    qgate = proj[:, :qh * 2 * dim].reshape(tokens, qh, 2 * dim)
+    kraw = proj[:, qh * 2 * dim:qh * 2 * dim + kh * dim].reshape(tokens, kh, dim)
+    wq = r.normal(0, 0.02, dim).astype(np.float32)
+    wk = r.normal(0, 0.02, dim).astype(np.float32)
+    cos, sin = oracle.rope_table(1e7, rotary, 2048)
+    eq = oracle.qk_norm_rope(np.ascontiguousarray(qgate[:, :, :dim]), wq, 1e-6, rotary, cos, sin,
+                             seq_len=7)
+    ek = oracle.qk_norm_rope(np.ascontiguousarray(kraw), wk, 1e-6, rotary, cos, sin, seq_len=7)
+    dproj = dev(proj)
+    dq = dproj[:, :qh * 2 * dim].view(tokens, qh, 2 * dim)[:, :, :dim]
+    dk = dproj[:, qh * 2 * dim:qh * 2 * dim + kh * dim].view(tokens, kh, dim)
+    dc, ds = q.rope_table(1e7, rotary, 2048, device="cuda")
+    gq, gk = q.native_q_k_norm_rope(dq, dk, dev(wq), dev(wk), 1e-6, rotary, dc, ds, seq_len=7,
+                                    q_out=nan_like((tokens, qh, dim)), k_out=nan_like((tokens, kh, dim)))
+    assert f32_close(gq, eq) and f32_close(gk, ek)

@@ -135,6 +135,25 @@ QDC_API int qdc_gather_rms_device_ids(qdc_ctx *ctx, void *out_x, void *out_y,
                               int centered, int64_t n, int64_t hidden,
                               int64_t vocab, int dtype, void *stream);
 
+/* qdc_gather_rms for callers that may not allocate device memory: no
+ * context, and no cudaMalloc / cudaFree or allocating library call, ever.
+ * No counterpart in the reference -- it exists for hosts whose memory
+ * manager owns every device byte (a CUDA.jl pool, a serving arena), loops
+ * that cannot take the device-wide synchronisation of cudaMalloc/cudaFree,
+ * and deployments with a memory budget fixed at start-up.  The ids are
+ * staged in a fixed 256 KiB array inside the library's device image, so a
+ * call takes at most 65536 ids (more: QDC_EINVAL).  Runs on the current
+ * device; its first call there looks the array up (cudaGetSymbolAddress),
+ * so make it before any stream capture.  All calls on a device share that
+ * array: calls whose work overlaps on the GPU race -- serialise them (calls
+ * on one stream are ordered).  Ids are validated on the host (QDC_EBOUNDS);
+ * errors are reported through qdc_last_error(NULL). */
+QDC_API int qdc_gather_rms_noalloc(void *out_x, void *out_y, const void *table,
+                                   const int32_t *ids, const void *add,
+                                   const float *gamma, float eps, int centered,
+                                   int64_t n, int64_t hidden, int64_t vocab,
+                                   int dtype, void *stream);
+
 /* Residual add + RMSNorm:  r = x + m (m NULL: r = x);  y = rms(r)*(1+g | g);
  * r stored when out_r != NULL.  One kernel covers
  *  - native_rms (src/backbone.jl:200-204, ext/cuda_workspace.jl:139-170):

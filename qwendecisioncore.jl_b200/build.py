@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 OUT_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(OUT_DIR, "libqdc_b200.so")
-SOURCES = [os.path.join(HERE, "csrc", "qdc_b200.cu")]
+SOURCES = [os.path.join(HERE, "csrc", "qdc_b200.cu"), os.path.join(HERE, "csrc", "qdc_noalloc.cu")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", "qdc_kernels.cuh"),
                   os.path.join(ROOT, "include", "qdc_b200.h")]
 

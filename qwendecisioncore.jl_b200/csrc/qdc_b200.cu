@@ -223,6 +223,10 @@ int gather_checks(qdc_ctx* ctx, const void* out_x, const void* out_y, const void
 
 }  // namespace
 
+// Lets the context-free entry point in qdc_noalloc.cu report through
+// qdc_last_error(NULL) (not exported).
+void qdc_set_thread_error(const char* msg) { t_err = msg; }
+
 // ====================================================================== ABI
 
 extern "C" {

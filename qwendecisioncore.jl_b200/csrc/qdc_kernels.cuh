@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_vec(SwigluArgs a) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads) swiglu_generic(SwigluArgs a) {
+static __global__ void __launch_bounds__(kThreads) swiglu_generic(SwigluArgs a) {
     pdl_enter();
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;

@@ -62,6 +62,7 @@ SIGNATURES = {
     "qdc_gather_rms": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _flt, _int, _i64, _i64, _i64, _int, _vp],
     "qdc_gather_rms_device_ids": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _flt, _int, _i64, _i64, _i64,
                                   _int, _vp],
+    "qdc_gather_rms_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _flt, _int, _i64, _i64, _i64, _int, _vp],
     "qdc_residual_rms": [_vp, _vp, _vp, _vp, _vp, _vp, _flt, _int, _i64, _i64, _i64, _i64, _i64,
                          _i64, _int, _vp],
     "qdc_qk_norm_rope": [_vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _vp, _flt, _int, _vp, _vp,

@@ -73,6 +73,14 @@ BYTES_PER_TOKEN = (BYTES["gather_rms"] + 18 * BYTES["gated_rms"]
 assert BYTES_PER_TOKEN == 2_392_064
 
 
+# DRAM bytes per token of the dominant kernel (SwiGLU, fp32 out), from the
+# ncu capture summarised in profiles/swiglu_tokens16384.md: dram__bytes_read
+# + dram__bytes_write = 653,557,760 B for 16,384 tokens.  Traffic grows in
+# proportion to the tokens (a pure stream), so a full launch's traffic is
+# this times its tokens.
+SWIGLU_DRAM_BYTES_PER_TOKEN = 653_557_760 / 16384
+
+
 def hbm_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -730,7 +738,12 @@ def main():
             "frac_of_hbm": round(value / (world * peak), 4),
             "roofline": {"bound": "hbm", "kernel": "swiglu (silu(gate)*up, 32768x3584-class rows)",
                          "achieved": round(dom_achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(dom_achieved / peak, 4), "traffic": None,
+                         "frac": round(dom_achieved / peak, 4),
+                         "traffic": round(T * SWIGLU_DRAM_BYTES_PER_TOKEN),
+                         "traffic_note": "dram read+write of one ncu capture at 16384 tokens "
+                                         "(profiles/swiglu_tokens16384.md) scaled to this launch's "
+                                         "tokens; reads equal the algorithmic reads, writes fall "
+                                         "short by output still dirty in L2 at kernel end",
                          "peak_kind": peak_kind,
                          "bytes_per_launch": dom_bytes, "us_per_launch": round(dom_us, 2)},
             "kernels": kern,

@@ -1,0 +1,96 @@
+"""Parity at the BASELINE full sizes (configs 2-5), kernel by kernel, against
+the oracle run multi-threaded on the host.  Each case also exercises the
+launch shape chosen for large unit counts."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def q(oracle):
+    import qdc_b200
+    oracle.set_threads(os.cpu_count() or 1)
+    yield qdc_b200
+    oracle.set_threads(1)
+
+
+def close(actual, expected, rtol=1e-5):
+    a = actual.detach().float().cpu().numpy().astype(np.float64) if torch.is_tensor(actual) else actual
+    e = np.asarray(expected, np.float64)
+    return bool((np.abs(a - e) <= 1e-6 + rtol * np.abs(e)).all())
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def test_config2_gather_residual_rms(q, oracle):
+    rng = np.random.default_rng(2)
+    table = rng.standard_normal((151936, 1024), dtype=np.float32) * np.float32(0.02)
+    ids = rng.integers(0, 151936, 16384).astype(np.int32)
+    m = rng.standard_normal((16384, 1024), dtype=np.float32)
+    w = rng.standard_normal(1024, dtype=np.float32) * np.float32(0.02)
+    ex_r, ex_y = oracle.gather_rms(table, ids, m, w, 1e-6)
+    x, y = q.native_gather_rms(dev(table), ids, dev(w), 1e-6, add=dev(m))
+    assert np.array_equal(x.cpu().numpy(), ex_r) and close(y, ex_y)
+    t16, m16 = oracle.bf16_encode(table), oracle.bf16_encode(m)
+    ex_r16, ex_y16 = oracle.gather_rms(t16, ids, m16, w, 1e-6)
+    b = lambda a: torch.from_numpy(a.view(np.int16)).cuda().view(torch.bfloat16)
+    x16, y16 = q.native_gather_rms(b(t16), ids, dev(w), 1e-6, add=b(m16))
+    dec = lambda t: oracle.bf16_decode(t.cpu().view(torch.int16).numpy().view(np.uint16))
+    assert close(dec(x16), oracle.bf16_decode(ex_r16), 1e-2)
+    assert close(dec(y16), oracle.bf16_decode(ex_y16), 1e-2)
+
+
+@pytest.mark.parametrize("tokens", [16384, 65536])
+def test_config3_and_5_qk_norm_rope(q, oracle, tokens):
+    rng = np.random.default_rng(tokens)
+    proj = rng.standard_normal((tokens, 8 * 512 + 2 * 2 * 256), dtype=np.float32)
+    qg = proj[:, :4096].reshape(tokens, 8, 512)
+    kr = proj[:, 4096:4608].reshape(tokens, 2, 256)
+    wq = rng.standard_normal(256, dtype=np.float32) * np.float32(0.02)
+    wk = rng.standard_normal(256, dtype=np.float32) * np.float32(0.02)
+    cos, sin = oracle.rope_table(1e7, 64, 2048)
+    eq = oracle.qk_norm_rope(np.ascontiguousarray(qg[:, :, :256]), wq, 1e-6, 64, cos, sin, seq_len=2048)
+    ek = oracle.qk_norm_rope(np.ascontiguousarray(kr), wk, 1e-6, 64, cos, sin, seq_len=2048)
+    dp = dev(proj)
+    dc, ds = q.rope_table(1e7, 64, 2048, device="cuda")
+    gq, gk = q.native_q_k_norm_rope(dp[:, :4096].view(tokens, 8, 512)[:, :, :256],
+                                    dp[:, 4096:4608].view(tokens, 2, 256), dev(wq), dev(wk), 1e-6, 64,
+                                    dc, ds, seq_len=2048)
+    assert close(gq, eq) and close(gk, ek)
+
+
+def test_config4_residual_rms_and_swiglu(q, oracle):
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((32768, 1024), dtype=np.float32)
+    m = rng.standard_normal((32768, 1024), dtype=np.float32)
+    w = rng.standard_normal(1024, dtype=np.float32) * np.float32(0.02)
+    ex_r, ex_y = oracle.residual_rms(x, m, w, 1e-6)
+    r, y = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6)
+    assert np.array_equal(r.cpu().numpy(), ex_r) and close(y, ex_y)
+    del x, m, r, y
+    g = rng.standard_normal((32768, 3584), dtype=np.float32)
+    u = rng.standard_normal((32768, 3584), dtype=np.float32)
+    e32, e16 = oracle.swiglu(g, u, want_bf16=True)
+    h32, h16 = q.native_mlp_gate(dev(g), dev(u), want_bf16=True)
+    assert close(h32, e32)
+    dec = oracle.bf16_decode(h16.cpu().view(torch.int16).numpy().view(np.uint16))
+    assert close(dec, oracle.bf16_decode(e16), 1e-2)
+
+
+def test_config5_gated_rms(q, oracle):
+    rng = np.random.default_rng(5)
+    T = 65536
+    o = rng.standard_normal((T, 16, 128), dtype=np.float32)
+    proj = rng.standard_normal((T, 8224), dtype=np.float32)
+    z = proj[:, 6144:8192].reshape(T, 16, 128)
+    w = (1 + rng.standard_normal(128, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    expected = oracle.gated_rms(o, np.ascontiguousarray(z), w, 1e-6)
+    dp = dev(proj)
+    got = q.native_gated_rms(dev(o), dp[:, 6144:8192].view(T, 16, 128), dev(w), 1e-6)
+    assert close(got, expected)

@@ -342,3 +342,46 @@ def test_q_k_norm_rope_one_launch(q, oracle, tokens, qh, kh, dim, rotary):
     gq, gk = q.native_q_k_norm_rope(dq, dk, dev(wq), dev(wk), 1e-6, rotary, dc, ds, seq_len=7,
                                     q_out=nan_like((tokens, qh, dim)), k_out=nan_like((tokens, kh, dim)))
     assert f32_close(gq, eq) and f32_close(gk, ek)
+
+
+def test_c_abi_rejects_bad_arguments_before_launch(q):
+    """Host-only fault tests through the raw C ABI: NULL pointers, bad sizes,
+    bad dtype, tables too short for the positions, aliasing -- each returns
+    QDC_EINVAL with a message and launches nothing."""
+    import ctypes
+    lib = q.load()
+    ctx = q.context(0)
+    h = ctx.handle
+    x = torch.zeros((4, 8), device="cuda")
+    y = torch.zeros((4, 8), device="cuda")
+    p = ctypes.c_void_p(x.data_ptr())
+    p2 = ctypes.c_void_p(y.data_ptr())
+    g = ctypes.c_void_p(torch.zeros(8, device="cuda").data_ptr())
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    EINVAL = 1
+    cases = [
+        lambda: lib.qdc_residual_rms(h, None, p2, None, None, g, 1e-6, 1, 4, 8, 8, 8, 8, 8, 0, s),  # x NULL
+        lambda: lib.qdc_residual_rms(h, None, p, p, None, g, 1e-6, 1, 4, 8, 8, 8, 8, 8, 0, s),  # y aliases x
+        lambda: lib.qdc_residual_rms(h, None, p2, p, None, g, 1e-6, 1, 4, 8, 4, 8, 8, 8, 0, s),  # ld < width
+        lambda: lib.qdc_residual_rms(h, None, p2, p, None, g, 1e-6, 1, 4, 8, 8, 8, 8, 8, 7, s),  # dtype
+        lambda: lib.qdc_residual_rms(h, None, p2, p, None, g, 1e-6, 1, -1, 8, 8, 8, 8, 8, 0, s),  # rows
+        lambda: lib.qdc_residual_rms(h, None, p2, p, None, None, 1e-6, 1, 4, 8, 8, 8, 8, 8, 0, s),  # gamma
+        lambda: lib.qdc_swiglu(h, None, None, p, p, 4, 8, 8, 8, 8, s),
+        lambda: lib.qdc_swiglu(h, p, None, None, p, 4, 8, 8, 8, 8, s),
+        lambda: lib.qdc_gated_rms(h, p, p, None, 4, 2, 4, 8, 8, 0, 8, g, 1e-6, s),
+        lambda: lib.qdc_gated_rms(h, p, p, p, 4, 2, 4, 8, 4, 0, 8, g, 1e-6, s),
+        lambda: lib.qdc_qk_norm_rope(h, p, p, 4, 2, 4, 8, 4, g, 1e-6, 3, p, p, 4, 0, 0, s),
+        lambda: lib.qdc_qk_norm_rope(h, p, p, 4, 2, 4, 8, 4, g, 1e-6, 4, p, p, 2, 0, 0, s),
+        lambda: lib.qdc_qk_norm_rope(h, p, p, 4, 2, 4, 8, 4, g, 1e-6, 4, None, None, 8, 0, 0, s),
+        lambda: lib.qdc_q_k_norm_rope(h, p, p, p, p, 4, 2, 0, 4, 8, 4, 8, 4, g, g, 1e-6, 0, None, None,
+                                      0, 0, 0, s),
+        lambda: lib.qdc_gather_rms_device_ids(h, p, None, None, p, None, None, 1e-6, 1, 4, 8, 64, 0, s),
+        lambda: lib.qdc_gather_rms_device_ids(h, None, None, p, p, None, None, 1e-6, 1, 4, 8, 64, 0, s),
+        lambda: lib.qdc_ws_alloc(h, 16, 100, ctypes.byref(ctypes.c_void_p())),
+        lambda: lib.qdc_ws_release(h, 1 << 40),
+    ]
+    for i, call in enumerate(cases):
+        assert call() == EINVAL, i
+        assert lib.qdc_last_error(h), i
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(x).item() == 0 and torch.count_nonzero(y).item() == 0  # nothing ran

@@ -323,6 +323,15 @@ def single_kernel(name, tokens, device, seed=1):
             q.native_q_k_norm_rope(qgate[:, :, :HEAD_DIM], kin, gq, gq, EPS, ROTARY, cos, sin,
                                    seq_len=SEQ, q_out=qo, k_out=ko, ctx=ctx)
         return both, 2 * (qo.numel() + ko.numel()) * 4 + table
+    if name == "delta_conv_norm":
+        proj = normal((T, PROJ_W))
+        conv = normal((QKV_W, 1, 4), 0.02)
+        qo = torch.empty((T, HK, DK), **f)
+        ko = torch.empty((T, HK, DK), **f)
+        vo = torch.empty((T, HV, DV), **f)
+        return (lambda: q.native_delta_conv_norm(proj, conv, HK, DK, HV, DV, seq_len=SEQ, q_out=qo,
+                                                 k_out=ko, v_out=vo, ctx=ctx),
+                2 * T * QKV_W * 4 + QKV_W * 16)
     raise SystemExit(f"unknown kernel {name}")
 
 
@@ -349,6 +358,8 @@ CONFIG_CASES = [  # (report name, kernel, tokens)
     ("cfg4_swiglu_f32", "swiglu", 32768),
     ("cfg4_swiglu_bf16", "swiglu_bf16", 32768),
     ("cfg4_swiglu_f32_and_bf16", "swiglu_both", 32768),
+    # the DeltaNet prologue (conv + SiLU + q/k L2 norms) at config-5 shapes
+    ("cfg5_delta_conv_norm", "delta_conv_norm", 32768),
 ]
 
 
@@ -541,7 +552,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the per-kernel configs 2-4")
     ap.add_argument("--kernel", default=None,
                     help="time one kernel alone (gather_rms[_bf16], post_rms[_bf16], swiglu, "
-                         "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope)")
+                         "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope, "
+                         "delta_conv_norm)")
     ap.add_argument("--tokens", type=int, default=16384, help="rows for --kernel")
     ap.add_argument("--no-forward", action="store_true", help="skip the whole-forward tokens/s leg")
     ap.add_argument("--forward-steps", type=int, default=2)

@@ -215,6 +215,23 @@ QDC_API int qdc_gated_rms(qdc_ctx *ctx, float *out, const float *o, const float 
                   int64_t z_off, int64_t out_ld, const float *gamma,
                   float eps, void *stream);
 
+/* DeltaNet prologue in one pass over the packed projection: 4-tap causal
+ * depthwise conv + SiLU on the [q | k | v] channels at the start of each
+ * token row (row t at proj + t*ld_proj), then q and k L2-normalised per head
+ * (q also divided by sqrt(key_dim)); eps is the reference's 1e-6.
+ * conv_w: [channels][4] (torch conv1d weight (C, 1, 4)).  Tokens are
+ * sequences of seq_len packed back to back (0: one sequence); the conv never
+ * reaches across a sequence start.  Outputs dense q, k [tokens][key_heads]
+ * [key_dim] and v [tokens][value_heads][value_dim].  Replaces
+ * causal_depthwise_kernel! + qk_normalize_kernel! (ext/cuda_delta.jl:8-40,
+ * 122-146; CPU src/backbone_cpu.jl:787-807, :411-427). */
+QDC_API int qdc_delta_conv_norm(qdc_ctx *ctx, float *q_out, float *k_out,
+                                float *v_out, const float *proj,
+                                int64_t ld_proj, const float *conv_w,
+                                int64_t tokens, int64_t seq_len, int key_heads,
+                                int key_dim, int value_heads, int value_dim,
+                                float eps, void *stream);
+
 /* SwiGLU gate:  h = silu(g) * u  (src/backbone.jl:196-197,352-355).
  * g/u rows at g + t*ld_g, u + t*ld_u (the packed [gate;up] projection of
  * ext/cuda_mlp.jl:63-71 is g = P, u = P + width, ld = 2*width).  Writes

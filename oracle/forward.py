@@ -4,9 +4,9 @@ TEST INFRASTRUCTURE ONLY.  It exists to pin the oracle's per-layer ops
 (oracle/qdc_oracle.c) against the reference's golden logits
 (test/fixtures/native/reference.json, checked at 2e-5 by the reference's
 test/backbone.jl:1-34): every norm / RoPE / gate / SwiGLU site of the
-forward runs through the C oracle, the out-of-scope parts (projections,
-causal attention, the 4-tap causal conv and the gated delta rule) run in
-float64 numpy.
+forward runs through the C oracle, as does the DeltaNet prologue (4-tap
+causal conv + SiLU + q/k L2 norms); the out-of-scope parts (projections,
+causal attention and the gated delta rule) run in float64 numpy.
 
 Reference call stack restated here (src/backbone.jl):
   backbone_hidden :433-460 -> native_gather :55-64 -> native_hidden_states
@@ -180,20 +180,6 @@ def _softplus(x):
     return np.maximum(x, 0.0) + np.log1p(np.exp(-np.abs(x)))
 
 
-def _causal_depthwise_silu(inp, weight):
-    """src/backbone.jl:264-276; weight (channels, 1, K) in torch layout."""
-    T, C = inp.shape
-    K = weight.shape[-1]
-    w = weight.reshape(C, K).astype(np.float64)
-    out = np.zeros((T, C))
-    for j in range(K):  # tap j multiplies input lagged by K-1-j
-        lag = K - 1 - j
-        if lag >= T:
-            continue
-        out[lag:] += inp[:T - lag] * w[:, j]
-    return out * _sigmoid(out)
-
-
 def full_attention(w, p, x, mask, cfg, trace=None):
     """src/backbone.jl:224-262 with the CPU q/k norm + RoPE of
     src/backbone_cpu.jl:113-136 (tables :90-105) through the oracle."""
@@ -234,11 +220,15 @@ def delta_attention(w, p, x, mask, cfg, trace=None):
     T = x.shape[0]
     kw = cfg.key_dim * cfg.key_heads
     masked = np.asarray(x, np.float64) * np.asarray(mask, np.float64)[:, None]
-    mixed = _causal_depthwise_silu(_linear(w[p + "linear_attn.in_proj_qkv.weight"], masked),
-                                   w[p + "linear_attn.conv1d.weight"])
-    q = mixed[:, :kw].reshape(T, cfg.key_heads, cfg.key_dim)
-    k = mixed[:, kw:2 * kw].reshape(T, cfg.key_heads, cfg.key_dim)
-    v = mixed[:, 2 * kw:].reshape(T, cfg.value_heads, cfg.value_dim)
+    qkv = _linear(w[p + "linear_attn.in_proj_qkv.weight"], masked).astype(np.float32)
+    conv = w[p + "linear_attn.conv1d.weight"]
+    # causal 4-tap conv + SiLU + q/k L2 norms through the oracle
+    # (src/backbone_cpu.jl:787-807, :411-427; generic src/backbone.jl:287-314)
+    q, k, v = O.delta_conv_norm(qkv, conv.reshape(conv.shape[0], conv.shape[-1]), cfg.key_heads,
+                                cfg.key_dim, cfg.value_heads, cfg.value_dim, seq_len=T)
+    if trace is not None:
+        trace.append(("delta_conv_norm", p, qkv, (q, k, v)))
+    q, k, v = q.astype(np.float64), k.astype(np.float64), v.astype(np.float64)
     z = _linear(w[p + "linear_attn.in_proj_z.weight"], masked).astype(np.float32)
     z = z.reshape(T, cfg.value_heads, cfg.value_dim)
     beta = _sigmoid(_linear(w[p + "linear_attn.in_proj_b.weight"], masked))
@@ -249,9 +239,7 @@ def delta_attention(w, p, x, mask, cfg, trace=None):
     result = np.empty((T, cfg.value_heads, cfg.value_dim))
     for h in range(cfg.value_heads):
         kh = h // groups
-        qh = q[:, kh, :] / (np.sqrt((q[:, kh, :] ** 2).sum(-1, keepdims=True) + 1e-6)
-                            * np.sqrt(cfg.key_dim))
-        kk = k[:, kh, :] / np.sqrt((k[:, kh, :] ** 2).sum(-1, keepdims=True) + 1e-6)
+        qh, kk = q[:, kh, :], k[:, kh, :]  # normalised by delta_conv_norm
         state = np.zeros((cfg.value_dim, cfg.key_dim))
         for t in range(T):
             f = np.exp(decay[t, h])

@@ -50,6 +50,8 @@ _SIGNATURES = {
     "qdo_gated_rms": (None, [_f32p, _f32p, _f32p, _i64, _int, _int, _i64, _i64,
                              _i64, _i64, _f32p, _flt]),
     "qdo_swiglu": (None, [_f32p, _u16p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64]),
+    "qdo_delta_conv_norm": (None, [_f32p, _f32p, _f32p, _f32p, _i64, _f32p, _i64, _i64, _int,
+                                   _int, _int, _int, _flt]),
 }
 
 
@@ -262,6 +264,23 @@ def swiglu(g, u, want_f32=True, want_bf16=False):
                      u.ctypes.data_as(_f32p), rows, width, _row_ld(g, 4), _row_ld(u, 4),
                      width)
     return out32, out16
+
+
+def delta_conv_norm(proj, conv_w, kh, kd, vh, vd, seq_len=None, eps=1e-6):
+    """DeltaNet prologue (qdc_oracle.h): proj (tokens, >= channels) rows with
+    unit inner stride, conv_w (channels, 4).  Returns q (tokens, kh, kd)
+    normalised, k (tokens, kh, kd) normalised, v (tokens, vh, vd)."""
+    assert proj.dtype == np.float32 and proj.ndim == 2
+    tokens = proj.shape[0]
+    C = 2 * kh * kd + vh * vd
+    w = _f32(conv_w).reshape(C, 4)
+    q = np.empty((tokens, kh, kd), np.float32)
+    k = np.empty((tokens, kh, kd), np.float32)
+    v = np.empty((tokens, vh, vd), np.float32)
+    if tokens:
+        lib().qdo_delta_conv_norm(_p(q), _p(k), _p(v), proj.ctypes.data_as(_f32p), _row_ld(proj, 4),
+                                  _p(w), tokens, int(seq_len or tokens), kh, kd, vh, vd, eps)
+    return q, k, v
 
 
 def silu(x):

@@ -290,6 +290,60 @@ void qdo_gated_rms(float *out, const float *o, const float *z, int64_t rows,
     }
 }
 
+/* ---- DeltaNet conv + SiLU + q/k L2 norm ---------------------------------- */
+
+static float conv4_silu(const float *proj, int64_t ld, const float *w, int64_t t,
+                        int64_t pos, int64_t c) {
+    /* cpu_convolution_four!, src/backbone_cpu.jl:787-807: value starts at
+     * the zero-filled output and takes the taps oldest first. */
+    float value = 0.0f;
+    for (int j = 0; j < 4; ++j) {
+        int64_t lag = 3 - j;
+        if (pos - lag < 0) continue;
+        value = value + proj[(t - lag) * ld + c] * w[c * 4 + j];
+    }
+    return qdo_silu(value);
+}
+
+void qdo_delta_conv_norm(float *q_out, float *k_out, float *v_out,
+                         const float *proj, int64_t ld, const float *conv_w,
+                         int64_t tokens, int64_t seq_len, int kh, int kd,
+                         int vh, int vd, float eps) {
+    const int64_t kw = (int64_t)kh * kd;
+    const float qmult = sqrtf((float)kd);
+#pragma omp parallel num_threads(g_threads) if (g_threads > 1)
+    {
+        float *buf = (float *)malloc((size_t)(kd > vd ? kd : vd) * sizeof(float));
+#pragma omp for schedule(static)
+        for (int64_t t = 0; t < tokens; ++t) {
+            int64_t pos = seq_len > 0 ? t % seq_len : t;
+            for (int g = 0; g < 2; ++g) {          /* q heads, then k heads */
+                float *out = g == 0 ? q_out : k_out;
+                float mult = g == 0 ? qmult : 1.0f;
+                for (int h = 0; h < kh; ++h) {
+                    int64_t base = g * kw + (int64_t)h * kd;
+                    double acc = 0.0;
+                    for (int i = 0; i < kd; ++i) {
+                        buf[i] = conv4_silu(proj, ld, conv_w, t, pos, base + i);
+                        acc += (double)buf[i] * (double)buf[i];
+                    }
+                    /* inv(sqrt(squared + 1f-6) * multiplier), :421 */
+                    float scale = 1.0f / (sqrtf((float)acc + eps) * mult);
+                    float *dst = out + (t * kh + h) * (int64_t)kd;
+                    for (int i = 0; i < kd; ++i) dst[i] = buf[i] * scale;
+                }
+            }
+            for (int h = 0; h < vh; ++h) {
+                int64_t base = 2 * kw + (int64_t)h * vd;
+                float *dst = v_out + (t * vh + h) * (int64_t)vd;
+                for (int i = 0; i < vd; ++i)
+                    dst[i] = conv4_silu(proj, ld, conv_w, t, pos, base + i);
+            }
+        }
+        free(buf);
+    }
+}
+
 /* ---- SwiGLU, src/backbone.jl:352-355 ------------------------------------ */
 
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,

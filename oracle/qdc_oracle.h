@@ -115,6 +115,21 @@ void qdo_gated_rms(float *out, const float *o, const float *z, int64_t rows,
                    int64_t z_off, int64_t out_ld, const float *weight,
                    float eps);
 
+/* DeltaNet prologue on the packed projection rows (channels
+ * [q (kh*kd) | k (kh*kd) | v (vh*vd)] at the start of each row, leading
+ * dimension ld): the 4-tap causal depthwise conv of src/backbone_cpu.jl:
+ * 787-807 (taps accumulated oldest first into a zero, each product and sum
+ * rounded; taps before the token's sequence start are absent), SiLU
+ * (src/backbone.jl:196-197), then the per-head L2 normalisation of
+ * src/backbone_cpu.jl:411-427 for q (multiplier sqrt(Float32(kd))) and k
+ * (multiplier 1): x * inv(sqrt(sum(x^2) + eps) * multiplier).  v is only
+ * activated.  Sequences of seq_len tokens are packed back to back.
+ * conv_w is [channels][4] (torch conv1d weight (C, 1, 4)). */
+void qdo_delta_conv_norm(float *q_out, float *k_out, float *v_out,
+                         const float *proj, int64_t ld, const float *conv_w,
+                         int64_t tokens, int64_t seq_len, int kh, int kd,
+                         int vh, int vd, float eps);
+
 /* SwiGLU, src/backbone.jl:352-355: h = silu(g) * u; optional fp32 and/or
  * bf16 (src/safetensors.jl:38-42) outputs. */
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,

@@ -49,8 +49,10 @@ def build(force=False, debug=False):
     with open(os.path.join(OUT_DIR, "ptxas.txt"), "w") as f:
         f.write(res.stdout + res.stderr)
     if res.returncode != 0:
-        sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building libqdc_b200.so")
+        noise = ("ptxas info", "    0 bytes stack", "ptxas info    : Function properties")
+        lines = [l for l in (res.stdout + res.stderr).splitlines() if not l.startswith(noise)]
+        sys.stderr.write("\n".join(lines) + "\n")
+        raise RuntimeError("nvcc failed building libqdc_b200.so (full log: _build/ptxas.txt)")
     return LIB
 
 

@@ -628,6 +628,80 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
     return launch_heads<true>(ctx, a, vec, stream, "gated_rms");
 }
 
+// ------------------------------------------------------- DeltaNet prologue
+
+int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj,
+                        int64_t ld_proj, const float* conv_w, int64_t tokens, int64_t seq_len,
+                        int key_heads, int key_dim, int value_heads, int value_dim, float eps,
+                        void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (tokens < 0 || key_heads < 1 || key_dim < 1 || value_heads < 1 || value_dim < 1 || seq_len < 0)
+        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d/%d dims=%d/%d", (long long)tokens,
+                    key_heads, value_heads, key_dim, value_dim);
+    const int64_t channels = 2 * int64_t(key_heads) * key_dim + int64_t(value_heads) * value_dim;
+    if (ld_proj < channels)
+        return fail(ctx, QDC_EINVAL, "ld_proj %lld < %lld channels", (long long)ld_proj, (long long)channels);
+    if (tokens == 0) return QDC_OK;
+    if (!q_out || !k_out || !v_out || !proj || !conv_w)
+        return fail(ctx, QDC_EINVAL, "outputs, proj and conv_w are required");
+    const int64_t per_tok = 2 * int64_t(key_heads) + value_heads;
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    const int64_t period = seq_len > 0 ? seq_len : tokens;
+    const qdc::FastDiv seq_div =
+        make_fastdiv(uint32_t(period < (int64_t(1) << 31) ? period : (int64_t(1) << 31)));
+    const bool aligned = aligned16(proj) && ld_proj % 4 == 0 && aligned16(conv_w) && aligned16(q_out) &&
+                         aligned16(k_out) && aligned16(v_out) && tokens < (int64_t(1) << 31);
+    // Shared-memory pipeline: 32-token x 4-head tiles, 3 stages (210 KB).
+    constexpr int PR = 32, PS = 3;
+    const int64_t groups = per_tok / 4;
+    const int64_t tiles = (tokens + PR - 1) / PR * groups;
+    if (aligned && key_dim == 128 && value_dim == 128 && per_tok % 4 == 0 &&
+        tiles < (int64_t(1) << 32) - (int64_t(1) << 24)) {
+        auto k = qdc::delta_conv_norm_pipe<PR, PS>;
+        const int smem = PS * (PR + 3) * 512 * int(sizeof(float));
+        static bool attr_set[64] = {};
+        if (ctx->device < 64 && !attr_set[ctx->device]) {
+            QDC_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr_set[ctx->device] = true;
+        }
+        qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
+                        value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),
+                        make_fastdiv(uint32_t(groups)), seq_div};
+        const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(grid));
+        cfg.blockDim = dim3(qdc::kConvPipeThreads);
+        cfg.dynamicSmemBytes = size_t(smem);
+        cfg.stream = static_cast<cudaStream_t>(stream);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, k, a);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch delta_conv_norm: %s", cudaGetErrorString(e));
+        return QDC_OK;
+    }
+    constexpr int R = 8;  // tokens per warp-unit on the register path
+    const int64_t runs = (tokens + R - 1) / R;
+    const bool vec = aligned && key_dim == 128 && value_dim == 128 &&
+                     runs * per_tok < (int64_t(1) << 32) - (int64_t(1) << 24);
+    qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
+                    value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)),
+                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div};
+    if (vec) {
+        auto k = qdc::delta_conv_norm_vec<R>;
+        const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32,
+                                  runs * per_tok);
+        return launch(ctx, k, grid, a, stream, "delta_conv_norm");
+    }
+    auto k = qdc::delta_conv_norm_generic;
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
+    return launch(ctx, k, grid, a, stream, "delta_conv_norm");
+}
+
 // ------------------------------------------------------------------ SwiGLU
 
 int qdc_swiglu(qdc_ctx* ctx, float* out_f32, uint16_t* out_bf16, const float* g, const float* u,

@@ -587,6 +587,281 @@ __global__ void __launch_bounds__(kThreads) head_norm_generic(HeadArgs a) {
     }
 }
 
+// ------------------------------------------------------- DeltaNet prologue
+// The Gated DeltaNet's row work between its projection GEMM and the delta
+// rule, in one pass over the packed projection (channels [q | k | v] at the
+// start of each token's row): the 4-tap causal depthwise conv (taps oldest
+// first, src/backbone_cpu.jl:787-807; taps before the token's sequence start
+// are absent), SiLU, and the per-head L2 normalisation of q (then divided by
+// sqrt(key_dim)) and k (src/backbone_cpu.jl:411-427).  The reference runs
+// these as three kernels (ext/cuda_delta.jl:8-40,122-146).
+
+struct ConvArgs {
+    float* q_out;        // [tokens][kh][kd]
+    float* k_out;        // [tokens][kh][kd]
+    float* v_out;        // [tokens][vh][vd]
+    const float* proj;   // token rows, leading dimension ld
+    const float* w;      // [channels][4]
+    int64_t ld, tokens, seq_len;
+    int kh, kd, vh, vd;
+    float eps;           // 1e-6 in the reference
+    float q_inv_mult;    // 1 / sqrt(Float32(kd))
+    uint32_t units;      // vector path: runs * heads; generic: tokens * heads
+    FastDiv heads_div;   // 2 kh + vh
+    FastDiv seq_div;     // seq_len (tokens when unset)
+};
+
+struct ConvHead {
+    int group;       // 0 q, 1 k, 2 v
+    int64_t c0;      // first channel of the head
+    int64_t head;    // head index inside its group
+};
+
+__device__ __forceinline__ ConvHead conv_head(const ConvArgs& a, int hh) {
+    ConvHead h;
+    h.group = hh < a.kh ? 0 : (hh < 2 * a.kh ? 1 : 2);
+    h.head = h.group == 0 ? hh : (h.group == 1 ? hh - a.kh : hh - 2 * a.kh);
+    h.c0 = h.group == 2 ? int64_t(2) * a.kh * a.kd + h.head * a.vd
+                        : int64_t(h.group) * a.kh * a.kd + h.head * a.kd;
+    return h;
+}
+
+__device__ __forceinline__ float* conv_dst(const ConvArgs& a, const ConvHead& h, int64_t t) {
+    if (h.group == 2) return a.v_out + (t * a.vh + h.head) * a.vd;
+    return (h.group == 0 ? a.q_out : a.k_out) + (t * a.kh + h.head) * a.kd;
+}
+
+// kd == vd == 128: one warp per (run of R tokens, head), 4 channels per lane.
+// The R + 3 rows the run needs are all loaded first; each token's conv then
+// reads its 4 taps from registers (rows t0-3..t0-1 are re-read by the
+// neighbouring run's warp, mostly from L2).
+template <int R>
+__global__ void __launch_bounds__(kThreads) delta_conv_norm_vec(ConvArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const uint32_t per_run = uint32_t(2 * a.kh + a.vh);
+    const uint32_t stride = gridDim.x * warps;
+    for (uint32_t u = blockIdx.x * warps + (threadIdx.x >> 5); u < a.units; u += stride) {
+        const uint32_t run = fdiv(u, a.heads_div);
+        const ConvHead h = conv_head(a, int(u - run * per_run));
+        const int64_t c = h.c0 + lane * 4;
+        const int64_t t0 = int64_t(run) * R;
+        float4 wt[4];  // taps 0..3 of channels c..c+3
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wt[i] = ld_nc_f4(a.w + (c + i) * 4);
+        float4 x[R + 3];
+#pragma unroll
+        for (int i = 0; i < R + 3; ++i) {
+            const int64_t t = t0 - 3 + i;
+            x[i] = (t >= 0 && t < a.tokens) ? ld_nc_f4(a.proj + t * a.ld + c) : make_float4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int64_t t = t0 + r;
+            if (t >= a.tokens) break;
+            const int pos = int(fmod(uint32_t(t), a.seq_div));
+            float4 acc = make_float4(0, 0, 0, 0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // tap j reads token t - 3 + j
+                if (pos >= 3 - j) {
+                    const float4 xv = x[r + j];
+                    acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, (&wt[0].x)[j]));
+                    acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, (&wt[1].x)[j]));
+                    acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, (&wt[2].x)[j]));
+                    acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, (&wt[3].x)[j]));
+                }
+            }
+            acc.x = silu(acc.x);
+            acc.y = silu(acc.y);
+            acc.z = silu(acc.z);
+            acc.w = silu(acc.w);
+            if (h.group < 2) {
+                float s = __fmaf_rn(acc.x, acc.x, 0.0f);
+                s = __fmaf_rn(acc.y, acc.y, s);
+                s = __fmaf_rn(acc.z, acc.z, s);
+                s = __fmaf_rn(acc.w, acc.w, s);
+                s = segment_sum<32>(s);
+                // inv(sqrt(sum + eps) * multiplier), src/backbone_cpu.jl:421
+                float scale = rsqrt_approx(__fadd_rn(s, a.eps));
+                if (h.group == 0) scale = __fmul_rn(scale, a.q_inv_mult);
+                acc.x = __fmul_rn(acc.x, scale);
+                acc.y = __fmul_rn(acc.y, scale);
+                acc.z = __fmul_rn(acc.z, scale);
+                acc.w = __fmul_rn(acc.w, scale);
+            }
+            st_f4(conv_dst(a, h, t) + lane * 4, acc);
+        }
+    }
+}
+
+// Multistage shared-memory pipeline (kd == vd == 128, 2 kh + vh divisible
+// by 4).  A tile is R tokens x 512 channels (4 heads): its R + 3 rows
+// (3 rows of halo for the taps) are copied global -> shared with 16-byte
+// cp.async while the previous STAGES-1 tiles are in flight, so each SM keeps
+// ~140 KB of loads outstanding without holding them in registers; the halo
+// rows are then read from shared memory instead of being fetched again.
+// 16 warps: warp w takes head w % 4 of the tile and tokens
+// [(w / 4) R/4, (w / 4 + 1) R/4).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int kConvPipeThreads = 512;
+
+template <int R, int STAGES>
+__global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(ConvArgs a) {
+    pdl_enter();
+    constexpr int CH = 512, ROWS = R + 3, TPW = R / 4;
+    extern __shared__ __align__(16) float stage_buf[];  // [STAGES][ROWS][CH]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t groups = uint32_t(2 * a.kh + a.vh) / 4;
+    const uint32_t tiles = a.units;  // runs * groups
+    auto issue = [&](uint32_t tile, int stage) {
+        const uint32_t run = fdiv(tile, a.heads_div);  // heads_div divides by `groups`
+        const uint32_t g = tile - run * groups;
+        const int64_t t0 = int64_t(run) * R - 3;
+        const float* src = a.proj + int64_t(g) * CH;
+        float* dst = stage_buf + stage * (ROWS * CH);
+        // thread tid copies 16-byte chunk (tid % 128) of rows tid / 128, +4, +8, ...
+        const int col = (tid % (CH / 4)) * 4;
+        constexpr int ROW_STEP = kConvPipeThreads / (CH / 4);
+        for (int row = tid / (CH / 4); row < ROWS; row += ROW_STEP) {
+            const int64_t t = t0 + row;
+            if (t >= 0 && t < a.tokens) cp_async16(dst + row * CH + col, src + t * a.ld + col);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        const uint32_t t = blockIdx.x + uint32_t(s) * gridDim.x;
+        if (t < tiles) issue(t, s);
+        cp_async_commit();
+    }
+    const int hq = warp & 3;
+    const int r0 = (warp >> 2) * TPW;
+    int stage = 0;
+    for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const uint32_t ahead = tile + uint32_t(STAGES - 1) * gridDim.x;
+        if (ahead < tiles) issue(ahead, (stage + STAGES - 1) % STAGES);
+        cp_async_commit();
+        cp_async_wait<STAGES - 1>();  // this tile's copies have landed
+        __syncthreads();
+        const uint32_t run = fdiv(tile, a.heads_div);
+        const uint32_t g = tile - run * groups;
+        const ConvHead h = conv_head(a, int(g * 4 + hq));
+        const int64_t c = h.c0 + lane * 4;
+        float4 wt[4];  // taps 0..3 of channels c..c+3
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wt[i] = *reinterpret_cast<const float4*>(a.w + (c + i) * 4);
+        // this warp's TPW tokens need TPW + 3 rows, all read once from shared memory
+        const float* buf = stage_buf + stage * (ROWS * CH) + r0 * CH + hq * 128 + lane * 4;
+        float4 xr[TPW + 3];
+#pragma unroll
+        for (int i = 0; i < TPW + 3; ++i) xr[i] = *reinterpret_cast<const float4*>(buf + i * CH);
+        const int64_t t_first = int64_t(run) * R + r0;
+        const int period = int(a.seq_div.d);
+        int pos = int(fmod(uint32_t(t_first), a.seq_div));
+        const int64_t dst_stride = h.group == 2 ? int64_t(a.vh) * a.vd : int64_t(a.kh) * a.kd;
+        float* dst = conv_dst(a, h, t_first) + lane * 4;
+#pragma unroll
+        for (int r = 0; r < TPW; ++r) {
+            if (t_first + r >= a.tokens) break;
+            float4 acc;
+            if (pos >= 3) {  // all four taps inside the sequence: one FMA chain per channel
+                acc.x = __fmul_rn(xr[r].x, wt[0].x);
+                acc.y = __fmul_rn(xr[r].y, wt[1].x);
+                acc.z = __fmul_rn(xr[r].z, wt[2].x);
+                acc.w = __fmul_rn(xr[r].w, wt[3].x);
+#pragma unroll
+                for (int j = 1; j < 4; ++j) {
+                    acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
+                    acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
+                    acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
+                    acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
+                }
+            } else {  // the first tokens of a sequence: taps before its start are absent
+                acc = make_float4(0, 0, 0, 0);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (pos >= 3 - j) {
+                        acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
+                        acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
+                        acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
+                        acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
+                    }
+                }
+            }
+            acc.x = silu(acc.x);
+            acc.y = silu(acc.y);
+            acc.z = silu(acc.z);
+            acc.w = silu(acc.w);
+            if (h.group < 2) {
+                float ss = __fmul_rn(acc.x, acc.x);
+                ss = __fmaf_rn(acc.y, acc.y, ss);
+                ss = __fmaf_rn(acc.z, acc.z, ss);
+                ss = __fmaf_rn(acc.w, acc.w, ss);
+                ss = segment_sum<32>(ss);
+                float scale = rsqrt_approx(__fadd_rn(ss, a.eps));
+                if (h.group == 0) scale = __fmul_rn(scale, a.q_inv_mult);
+                acc.x = __fmul_rn(acc.x, scale);
+                acc.y = __fmul_rn(acc.y, scale);
+                acc.z = __fmul_rn(acc.z, scale);
+                acc.w = __fmul_rn(acc.w, scale);
+            }
+            st_f4(dst + r * dst_stride, acc);
+            pos = pos + 1 == period ? 0 : pos + 1;
+        }
+        __syncthreads();  // every warp is done with this stage before it is refilled
+        stage = (stage + 1) % STAGES;
+    }
+    cp_async_wait<0>();
+}
+
+// Any head widths / alignment: warp per (token, head); the conv is recomputed
+// in the normalising second pass.
+static __global__ void __launch_bounds__(kThreads) delta_conv_norm_generic(ConvArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t per_tok = 2 * a.kh + a.vh;
+    const int64_t units = a.tokens * per_tok;
+    for (int64_t u = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); u < units;
+         u += int64_t(gridDim.x) * warps) {
+        const int64_t t = u / per_tok;
+        const ConvHead h = conv_head(a, int(u - t * per_tok));
+        const int64_t pos = a.seq_len > 0 ? t % a.seq_len : t;
+        const int width = h.group == 2 ? a.vd : a.kd;
+        auto conv = [&](int i) {
+            const int64_t c = h.c0 + i;
+            float acc = 0.0f;
+            for (int j = 0; j < 4; ++j)
+                if (pos >= 3 - j)
+                    acc = __fadd_rn(acc, __fmul_rn(__ldg(a.proj + (t - 3 + j) * a.ld + c),
+                                                   __ldg(a.w + c * 4 + j)));
+            return silu(acc);
+        };
+        float scale = 1.0f;
+        if (h.group < 2) {
+            float s = 0.0f;
+            for (int i = lane; i < width; i += 32) {
+                const float v = conv(i);
+                s = __fmaf_rn(v, v, s);
+            }
+            s = segment_sum<32>(s);
+            scale = rsqrt_approx(__fadd_rn(s, a.eps));
+            if (h.group == 0) scale = __fmul_rn(scale, a.q_inv_mult);
+        }
+        float* dst = conv_dst(a, h, t);
+        for (int i = lane; i < width; i += 32) dst[i] = h.group < 2 ? __fmul_rn(conv(i), scale) : conv(i);
+    }
+}
+
 // ---------------------------------------------------------------- SwiGLU
 
 struct SwigluArgs {

@@ -70,6 +70,8 @@ SIGNATURES = {
     "qdc_q_k_norm_rope": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _i64, _i64,
                           _vp, _vp, _flt, _int, _vp, _vp, _i64, _i64, _i64, _vp],
     "qdc_gated_rms": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _vp],
+    "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
+                            _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],
 }
 _RESTYPES = {"qdc_status_string": ctypes.c_char_p, "qdc_last_error": ctypes.c_char_p}

@@ -15,9 +15,9 @@ Per layer (native_layer, src/backbone.jl:363-382):
                   layer's MLP residual add (qdc_residual_rms)
   attention    -- full: one [q;k;v] GEMM, qdc q/k norm + partial RoPE,
                   causal GQA attention (torch SDPA), sigmoid gate, o GEMM;
-                  delta: one [qkv;z;a;b] GEMM, causal 4-tap conv + SiLU, q/k
-                  L2 norms, gates, chunked gated delta rule (torch), qdc gated
-                  norm reading z in place, out GEMM
+                  delta: one [qkv;z;a;b] GEMM, qdc causal 4-tap conv + SiLU +
+                  q/k L2 norms, gates, chunked gated delta rule (torch), qdc
+                  gated norm reading z in place, out GEMM
   post norm    -- qdc residual add + RMSNorm
   MLP          -- one [gate;up] GEMM, qdc SwiGLU, down GEMM
   residual add -- fused with the next layer's input norm / the final norm.
@@ -26,7 +26,6 @@ The projections, attention, conv and delta rule are the reference's
 out-of-scope parts; they run as plain torch Float32 ops (cuBLAS GEMMs with
 TF32 disabled, as the reference computes in Float32, src/backbone.jl:14-16).
 """
-import math
 
 import numpy as np
 import torch
@@ -139,19 +138,14 @@ class QwenBackbone:
         kw, vw, C = cfg.key_width, cfg.value_width, cfg.qkv_width
         masked = y * mask.view(T, 1).to(torch.float32)
         proj = masked @ layer["proj"].t()  # [qkv | z | a | b] per token
-        qkv = proj[:, :C].view(B, S, C)
-        # causal depthwise conv, taps accumulated oldest first (src/backbone_cpu.jl:787-807)
-        Kt = layer["conv"].shape[1]
-        padded = F.pad(qkv, (0, 0, Kt - 1, 0))
-        acc = padded[:, 0:S] * layer["conv"][:, 0]
-        for j in range(1, Kt):
-            acc = acc + padded[:, j:j + S] * layer["conv"][:, j]
-        mixed = acc * torch.sigmoid(acc)
-        q = mixed[..., :kw].reshape(B, S, cfg.key_heads, cfg.key_dim)
-        k = mixed[..., kw:2 * kw].reshape(B, S, cfg.key_heads, cfg.key_dim)
-        v = mixed[..., 2 * kw:].reshape(B, S, cfg.value_heads, cfg.value_dim)
-        q = q / (torch.sqrt((q * q).sum(-1, keepdim=True) + 1e-6) * math.sqrt(cfg.key_dim))
-        k = k / torch.sqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+        # causal 4-tap conv + SiLU + q/k L2 norms in one qdc pass over the
+        # projection (src/backbone.jl:287-314)
+        q, k, v = ops.native_delta_conv_norm(proj, layer["conv"], cfg.key_heads, cfg.key_dim,
+                                             cfg.value_heads, cfg.value_dim, seq_len=S, ctx=self.ctx)
+        self._record("delta_conv_norm", (proj[:, :C], layer["conv"]), (q, k, v))
+        q = q.view(B, S, cfg.key_heads, cfg.key_dim)
+        k = k.view(B, S, cfg.key_heads, cfg.key_dim)
+        v = v.view(B, S, cfg.value_heads, cfg.value_dim)
         a = proj[:, C + vw:C + vw + cfg.value_heads].view(B, S, cfg.value_heads)
         b = proj[:, C + vw + cfg.value_heads:C + vw + 2 * cfg.value_heads].view(B, S, cfg.value_heads)
         beta = torch.sigmoid(b)

@@ -13,6 +13,8 @@ for CuArrays and the work done by the library's sm_100a kernels:
                        src/backbone.jl:206-235 (CPU form src/backbone_cpu.jl:113-136)
   native_q_k_norm_rope the same for the query and key heads in one launch
   native_gated_rms     src/backbone.jl:339-341, ext/cuda_delta.jl:99-116
+  native_delta_conv_norm  conv + SiLU + q/k L2 norms of delta_attention,
+                       src/backbone.jl:287-314, ext/cuda_delta.jl:8-40,122-146
   native_mlp_gate      src/backbone.jl:352-355, ext/cuda_mlp.jl:49-61
   rope_table           src/backbone_cpu.jl:90-105
 
@@ -422,6 +424,43 @@ def native_gated_rms(o, z, weight, eps, *, out=None, ctx=None, stream=None):
                                     z_ld, 0, ld_out, _ptr(weight), float(eps), _stream(dev, stream)),
               ctx.handle)
     return out
+
+
+def native_delta_conv_norm(proj, conv_w, key_heads, key_dim, value_heads, value_dim, *, seq_len=None,
+                           eps=1e-6, q_out=None, k_out=None, v_out=None, ctx=None, stream=None):
+    """The Gated DeltaNet's row work after its projection GEMM, in one pass:
+    causal 4-tap depthwise conv + SiLU over the [q | k | v] channels at the
+    start of each row of `proj` (tokens, >= channels), then per-head L2
+    normalisation of q (also / sqrt(key_dim)) and k
+    (src/backbone.jl:287-314; CPU src/backbone_cpu.jl:787-807, :411-427).
+    Sequences of `seq_len` tokens are packed back to back.  conv_w:
+    (channels, 4) or the torch (channels, 1, 4).  Returns dense q, k
+    (tokens, key_heads, key_dim) and v (tokens, value_heads, value_dim)."""
+    dev = _cuda(proj, conv_w, q_out, k_out, v_out)
+    tokens, width, ld = _rows(proj, "proj")
+    C = 2 * key_heads * key_dim + value_heads * value_dim
+    if width < C:
+        raise DimensionMismatch(_lib.QDC_EINVAL, f"projection has {width} < {C} channels")
+    if proj.dtype != torch.float32 or conv_w.dtype != torch.float32:
+        raise ArgumentError(_lib.QDC_EINVAL, "DeltaNet prologue takes Float32 tensors")
+    w = conv_w.reshape(conv_w.shape[0], conv_w.shape[-1]).contiguous()
+    if tuple(w.shape) != (C, 4):
+        raise DimensionMismatch(_lib.QDC_EINVAL, f"conv weight must be ({C}, 4), got {tuple(conv_w.shape)}")
+    f = dict(dtype=torch.float32, device=dev)
+    q_out = torch.empty((tokens, key_heads, key_dim), **f) if q_out is None else q_out
+    k_out = torch.empty((tokens, key_heads, key_dim), **f) if k_out is None else k_out
+    v_out = torch.empty((tokens, value_heads, value_dim), **f) if v_out is None else v_out
+    for t, shape in ((q_out, (tokens, key_heads, key_dim)), (k_out, (tokens, key_heads, key_dim)),
+                     (v_out, (tokens, value_heads, value_dim))):
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise DimensionMismatch(_lib.QDC_EINVAL, "output shape differs")
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_delta_conv_norm(ctx.handle, _ptr(q_out), _ptr(k_out), _ptr(v_out), _ptr(proj),
+                                          ld, _ptr(w), tokens, int(seq_len or 0), key_heads, key_dim,
+                                          value_heads, value_dim, float(eps), _stream(dev, stream)),
+              ctx.handle)
+    return q_out, k_out, v_out
 
 
 def native_mlp_gate(gate, up, *, want_f32=True, want_bf16=False, out_f32=None, out_bf16=None,

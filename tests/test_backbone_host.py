@@ -59,6 +59,12 @@ def cpu_backbone(monkeypatch, oracle):
     def swiglu(g, u, ctx=None, **k):
         return T(oracle.swiglu(c(n(g)), c(n(u)))[0]), None
 
+    def conv_norm(proj, w, kh, kd, vh, vd, seq_len=None, ctx=None, **k):
+        C = 2 * kh * kd + vh * vd
+        q, kk, v = oracle.delta_conv_norm(c(n(proj))[:, :C], n(w).reshape(C, 4), kh, kd, vh, vd,
+                                          seq_len=seq_len)
+        return T(q), T(kk), T(v)
+
     def rope_table(theta, r, rows, device=None):
         cs, sn = oracle.rope_table(theta, r, rows)
         return T(cs), T(sn)
@@ -66,6 +72,7 @@ def cpu_backbone(monkeypatch, oracle):
     for name, fn in (("native_gather_rms", gather_rms), ("native_residual_rms", residual_rms),
                      ("native_residual_add_rms", residual_add_rms), ("native_q_k_norm_rope", q_k),
                      ("native_gated_rms", gated), ("native_mlp_gate", swiglu),
+                     ("native_delta_conv_norm", conv_norm),
                      ("rope_table", rope_table)):
         monkeypatch.setattr(ops, name, fn)
 

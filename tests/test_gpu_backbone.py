@@ -139,6 +139,7 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
     assert kinds.count("swiglu") == n_layers and kinds.count("gated_rms") == 3
     assert kinds.count("q_norm_rope") == 1 and kinds.count("k_norm_rope") == 1
     assert kinds.count("mlp_rms") == n_layers - 1 and kinds.count("final_rms") == 1
+    assert kinds.count("delta_conv_norm") == 3
     w = omodel.weights
     cos, sin = oracle.rope_table(cfg.rope_theta, cfg.rotary_dim, 64)
     layer = 0
@@ -162,6 +163,12 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
             ex = oracle.qk_norm_rope(np.ascontiguousarray(x), gam, cfg.eps, cfg.rotary_dim, cos, sin,
                                      seq_len=64)
             assert close(cpu(outs[0]), ex), site
+        elif site == "delta_conv_norm":
+            C = 2 * cfg.key_heads * cfg.key_dim + cfg.value_heads * cfg.value_dim
+            eq, ek, ev = oracle.delta_conv_norm(np.ascontiguousarray(cpu(ins[0])),
+                                                cpu(ins[1]).reshape(C, 4), cfg.key_heads, cfg.key_dim,
+                                                cfg.value_heads, cfg.value_dim, seq_len=64)
+            assert close(cpu(outs[0]), eq) and close(cpu(outs[1]), ek) and close(cpu(outs[2]), ev)
         elif site == "gated_rms":
             o, z = cpu(ins[0]), np.ascontiguousarray(cpu(ins[1]))
             ex = oracle.gated_rms(o, z, w[p + "linear_attn.norm.weight"], cfg.eps)

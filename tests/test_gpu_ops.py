@@ -385,3 +385,25 @@ def test_c_abi_rejects_bad_arguments_before_launch(q):
         assert lib.qdc_last_error(h), i
     torch.cuda.synchronize()
     assert torch.count_nonzero(x).item() == 0 and torch.count_nonzero(y).item() == 0  # nothing ran
+
+
+# ------------------------------------------------------- DeltaNet prologue
+
+@pytest.mark.parametrize("tokens,seq_len,kh,kd,vh,vd,pad", [
+    (200, 64, 2, 128, 4, 128, 8),      # config 1 shape, vector path
+    (130, 0, 16, 128, 16, 128, 16),    # config 5 heads, one sequence, tail run
+    (37, 10, 2, 128, 2, 128, 0),       # sequences shorter than a run
+    (9, 3, 1, 2, 2, 2, 7),             # fixture dims, generic path
+    (50, 25, 2, 64, 3, 96, 4),         # generic head widths
+    (1, 0, 2, 128, 4, 128, 8),
+])
+def test_delta_conv_norm(q, oracle, tokens, seq_len, kh, kd, vh, vd, pad):
+    r = rng(tokens + kd + vd)
+    C = 2 * kh * kd + vh * vd
+    proj = r.normal(0, 1, (tokens, C + pad)).astype(np.float32)
+    w = r.normal(0, 0.5, (C, 1, 4)).astype(np.float32)
+    eq, ek, ev = oracle.delta_conv_norm(proj, w.reshape(C, 4), kh, kd, vh, vd, seq_len=seq_len or None)
+    gq, gk, gv = q.native_delta_conv_norm(dev(proj), dev(w), kh, kd, vh, vd, seq_len=seq_len or None,
+                                          q_out=nan_like((tokens, kh, kd)), k_out=nan_like((tokens, kh, kd)),
+                                          v_out=nan_like((tokens, vh, vd)))
+    assert f32_close(gq, eq) and f32_close(gk, ek) and f32_close(gv, ev)

@@ -72,6 +72,15 @@ QDC_API const char *qdc_status_string(int status);
 QDC_API int qdc_init(int device, qdc_ctx **out);
 QDC_API int qdc_destroy(qdc_ctx *ctx);
 
+/* Context options (value 0 = off, nonzero = on); QDC_EINVAL for an unknown
+ * option.
+ * QDC_OPT_PDL (default on): launch this context's kernels with programmatic
+ * dependent launch, so each overlaps its launch and ramp with the preceding
+ * kernel's drain; every kernel still waits for its predecessor grid to
+ * complete before it touches global memory. */
+#define QDC_OPT_PDL 1
+QDC_API int qdc_set_option(qdc_ctx *ctx, int option, int value);
+
 /* Text of the last failure on this context (or on this thread, ctx NULL). */
 QDC_API const char *qdc_last_error(const qdc_ctx *ctx);
 
@@ -214,6 +223,20 @@ QDC_API int qdc_gated_rms(qdc_ctx *ctx, float *out, const float *o, const float 
                   int64_t rows, int heads, int dim, int64_t o_ld, int64_t z_ld,
                   int64_t z_off, int64_t out_ld, const float *gamma,
                   float eps, void *stream);
+
+/* Attention output gate: out[t][h][:] = values * sigmoid(gate) with
+ * sigmoid(x) = inv(1 + exp(-x)) (src/backbone.jl:258-259).  values element
+ * (b, h, s, d) at values + b*v_b + h*v_h + s*v_s + d -- the (batch, heads,
+ * seq, dim) output of an attention kernel, read in place; gate at
+ * gate + t*g_t + h*g_h + d with t = b*seq + s (the gate half of the packed
+ * [q;gate] projection: g_t = heads*2*dim, g_h = 2*dim, base + dim); out at
+ * out + t*out_t + h*dim + d.  Replaces merge_gate_kernel!
+ * (ext/cuda_attention.jl:92-108) and the transpose before it. */
+QDC_API int qdc_attn_gate(qdc_ctx *ctx, float *out, const float *values,
+                          const float *gate, int64_t batch, int64_t seq,
+                          int heads, int dim, int64_t v_b, int64_t v_h,
+                          int64_t v_s, int64_t g_t, int64_t g_h, int64_t out_t,
+                          void *stream);
 
 /* DeltaNet prologue in one pass over the packed projection: 4-tap causal
  * depthwise conv + SiLU on the [q | k | v] channels at the start of each

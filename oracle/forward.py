@@ -201,16 +201,18 @@ def full_attention(w, p, x, mask, cfg, trace=None):
     allowed = (i <= j) & (np.asarray(mask)[:, None] == 1)
     bias = np.where(allowed, 0.0, -FLOATMAX32)
     groups = Hq // Hkv
-    out = np.empty((T, Hq * D))
+    values = np.empty((1, Hq, T, D), np.float32)
     for h in range(Hq):
         kv = h // groups
         scores = (k[:, kv, :].astype(np.float64) @ q[:, h, :].astype(np.float64).T) / np.sqrt(D)
         scores = scores + bias  # (keys, queries)
         probs = np.exp(scores - scores.max(axis=0, keepdims=True))
         probs /= probs.sum(axis=0, keepdims=True)
-        values = probs.T @ v[:, kv, :]  # (queries, D)
-        gate = _sigmoid(qgate[:, h, D:].astype(np.float64))
-        out[:, h * D:(h + 1) * D] = values * gate
+        values[0, h] = (probs.T @ v[:, kv, :]).astype(np.float32)  # (queries, D)
+    # values .* native_sigmoid.(gate) through the oracle (src/backbone.jl:258-259)
+    out = O.attn_gate(values, qgate[:, :, D:])
+    if trace is not None:
+        trace.append(("attn_gate", p, (values, qgate[:, :, D:]), out))
     return _linear(w[p + "self_attn.o_proj.weight"], out)
 
 

@@ -50,6 +50,8 @@ _SIGNATURES = {
     "qdo_gated_rms": (None, [_f32p, _f32p, _f32p, _i64, _int, _int, _i64, _i64,
                              _i64, _i64, _f32p, _flt]),
     "qdo_swiglu": (None, [_f32p, _u16p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64]),
+    "qdo_attn_gate": (None, [_f32p, _f32p, _f32p, _i64, _i64, _int, _int, _i64, _i64, _i64, _i64,
+                             _i64, _i64]),
     "qdo_delta_conv_norm": (None, [_f32p, _f32p, _f32p, _f32p, _i64, _f32p, _i64, _i64, _int,
                                    _int, _int, _int, _flt]),
 }
@@ -281,6 +283,22 @@ def delta_conv_norm(proj, conv_w, kh, kd, vh, vd, seq_len=None, eps=1e-6):
         lib().qdo_delta_conv_norm(_p(q), _p(k), _p(v), proj.ctypes.data_as(_f32p), _row_ld(proj, 4),
                                   _p(w), tokens, int(seq_len or tokens), kh, kd, vh, vd, eps)
     return q, k, v
+
+
+def attn_gate(values, gate):
+    """values (batch, heads, seq, dim) float32 view (unit inner stride), gate
+    (batch*seq, heads, dim) view.  Returns out (batch*seq, heads*dim):
+    values * sigmoid(gate), src/backbone.jl:258-259."""
+    B, H, S, D = values.shape
+    assert values.dtype == np.float32 and values.strides[3] == 4
+    assert gate.shape == (B * S, H, D) and gate.dtype == np.float32 and gate.strides[2] == 4
+    out = np.empty((B * S, H * D), np.float32)
+    if out.size:
+        st = [x // 4 for x in values.strides]
+        lib().qdo_attn_gate(_p(out), values.ctypes.data_as(_f32p), gate.ctypes.data_as(_f32p), B, S,
+                            H, D, st[0], st[1], st[2], gate.strides[0] // 4, gate.strides[1] // 4,
+                            H * D)
+    return out
 
 
 def silu(x):

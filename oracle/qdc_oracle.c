@@ -344,6 +344,25 @@ void qdo_delta_conv_norm(float *q_out, float *k_out, float *v_out,
     }
 }
 
+/* ---- attention output gate, src/backbone.jl:258-259 ----------------------- */
+
+void qdo_attn_gate(float *out, const float *values, const float *gate,
+                   int64_t batch, int64_t seq, int heads, int dim, int64_t v_b,
+                   int64_t v_h, int64_t v_s, int64_t g_t, int64_t g_h,
+                   int64_t out_t) {
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
+    for (int64_t t = 0; t < batch * seq; ++t) {
+        int64_t b = t / seq, s = t % seq;
+        for (int h = 0; h < heads; ++h)
+            for (int d = 0; d < dim; ++d) {
+                float g = gate[t * g_t + (int64_t)h * g_h + d];
+                float sig = 1.0f / (1.0f + expf(-g)); /* native_sigmoid, :196 */
+                out[t * out_t + (int64_t)h * dim + d] =
+                    values[b * v_b + (int64_t)h * v_h + s * v_s + d] * sig;
+            }
+    }
+}
+
 /* ---- SwiGLU, src/backbone.jl:352-355 ------------------------------------ */
 
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,

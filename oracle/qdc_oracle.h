@@ -130,6 +130,16 @@ void qdo_delta_conv_norm(float *q_out, float *k_out, float *v_out,
                          int64_t tokens, int64_t seq_len, int kh, int kd,
                          int vh, int vd, float eps);
 
+/* Attention output gate, src/backbone.jl:258-259 (src/backbone_cpu.jl:55-56):
+ * out[t][h][d] = values * inv(1 + exp(-gate)).  values element (b, h, s, d)
+ * at values + b*v_b + h*v_h + s*v_s + d (t = b*seq + s); gate at
+ * gate + t*g_t + h*g_h + d (the gate half of the packed [q;gate] rows);
+ * out at out + t*out_t + h*dim + d. */
+void qdo_attn_gate(float *out, const float *values, const float *gate,
+                   int64_t batch, int64_t seq, int heads, int dim, int64_t v_b,
+                   int64_t v_h, int64_t v_s, int64_t g_t, int64_t g_h,
+                   int64_t out_t);
+
 /* SwiGLU, src/backbone.jl:352-355: h = silu(g) * u; optional fp32 and/or
  * bf16 (src/safetensors.jl:38-42) outputs. */
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,

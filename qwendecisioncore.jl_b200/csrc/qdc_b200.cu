@@ -21,6 +21,7 @@
 struct qdc_ctx {
     int device = -1;
     int sm_count = 0;
+    bool pdl = true;  // QDC_OPT_PDL
     std::string err;
     // workspace arena
     char* arena = nullptr;
@@ -121,20 +122,21 @@ int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int
     return int(g < 1 ? 1 : g);
 }
 
-// Launch with programmatic stream serialization (see qdc_kernels.cuh).
+// Launch, with programmatic stream serialization unless the context turned
+// it off (QDC_OPT_PDL; see qdc_kernels.cuh).
 template <typename Args>
 int launch(qdc_ctx* ctx, void (*kernel)(Args), int grid, const Args& args, void* stream,
-           const char* name) {
+           const char* name, int threads = qdc::kThreads, size_t smem = 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid));
-    cfg.blockDim = dim3(qdc::kThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.blockDim = dim3(unsigned(threads));
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.attrs = ctx->pdl ? attr : nullptr;
+    cfg.numAttrs = ctx->pdl ? 1 : 0;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch %s: %s", name, cudaGetErrorString(e));
@@ -293,6 +295,14 @@ int qdc_destroy(qdc_ctx* ctx) {
     }
     delete ctx;
     return QDC_OK;
+}
+
+int qdc_set_option(qdc_ctx* ctx, int option, int value) {
+    if (int s = check_ctx(ctx)) return s;
+    switch (option) {
+        case QDC_OPT_PDL: ctx->pdl = value != 0; return QDC_OK;
+        default: return fail(ctx, QDC_EINVAL, "unknown option %d", option);
+    }
 }
 
 int qdc_sync(qdc_ctx* ctx, void* stream) {
@@ -628,6 +638,42 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
     return launch_heads<true>(ctx, a, vec, stream, "gated_rms");
 }
 
+// ------------------------------------------------------ attention out gate
+
+int qdc_attn_gate(qdc_ctx* ctx, float* out, const float* values, const float* gate, int64_t batch,
+                  int64_t seq, int heads, int dim, int64_t v_b, int64_t v_h, int64_t v_s, int64_t g_t,
+                  int64_t g_h, int64_t out_t, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (batch < 0 || seq < 0 || heads < 1 || dim < 1)
+        return fail(ctx, QDC_EINVAL, "bad sizes batch=%lld seq=%lld heads=%d dim=%d", (long long)batch,
+                    (long long)seq, heads, dim);
+    const int64_t units = batch * seq * heads;
+    if (units == 0) return QDC_OK;
+    if (!out || !values || !gate) return fail(ctx, QDC_EINVAL, "out, values and gate are required");
+    if (out_t < int64_t(heads) * dim || v_b < 0 || v_h < 0 || v_s < 0 || g_t < 0 || g_h < 0)
+        return fail(ctx, QDC_EINVAL, "bad strides");
+    if (units >= (int64_t(1) << 32) - (int64_t(1) << 24))
+        return fail(ctx, QDC_EINVAL, "too many (token, head) units");
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    qdc::GateArgs a{out, values, gate, seq, heads, dim, v_b, v_h, v_s, g_t, g_h, out_t, uint32_t(units),
+                    make_fastdiv(uint32_t(heads)), make_fastdiv(uint32_t(seq))};
+    const bool vec = dim % 128 == 0 && dim <= 512 && aligned16(out) && aligned16(values) &&
+                     aligned16(gate) && v_b % 4 == 0 && v_h % 4 == 0 && v_s % 4 == 0 && g_t % 4 == 0 &&
+                     g_h % 4 == 0 && out_t % 4 == 0 && seq < (int64_t(1) << 31);
+    void (*k)(qdc::GateArgs) = qdc::attn_gate_generic;
+    if (vec) {
+        switch (dim / 128) {
+            case 1: k = qdc::attn_gate_vec<1>; break;
+            case 2: k = qdc::attn_gate_vec<2>; break;
+            case 4: k = qdc::attn_gate_vec<4>; break;
+            default: break;
+        }
+    }
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, units);
+    return launch(ctx, k, grid, a, stream, "attn_gate");
+}
+
 // ------------------------------------------------------- DeltaNet prologue
 
 int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj,
@@ -669,20 +715,8 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
                         value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),
                         make_fastdiv(uint32_t(groups)), seq_div};
         const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(unsigned(grid));
-        cfg.blockDim = dim3(qdc::kConvPipeThreads);
-        cfg.dynamicSmemBytes = size_t(smem);
-        cfg.stream = static_cast<cudaStream_t>(stream);
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, k, a);
-        if (e == cudaSuccess) e = cudaGetLastError();
-        if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch delta_conv_norm: %s", cudaGetErrorString(e));
-        return QDC_OK;
+        return launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
+                      size_t(smem));
     }
     constexpr int R = 8;  // tokens per warp-unit on the register path
     const int64_t runs = (tokens + R - 1) / R;

@@ -28,12 +28,13 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kThreads = 256;  // 8 warps per CTA for the vector kernels
 
 // ------------------------------------------------ programmatic dependent launch
-// Kernels are launched with programmatic stream serialization: a kernel's CTAs
-// may become resident while its predecessor drains.  Each kernel first waits
-// for the predecessor grid to complete (griddepcontrol.wait -- a no-op when
-// launched without the attribute) and only then touches global memory, then
-// lets its own successor start launching.  This hides the launch and ramp
-// of each of the ~100 kernels of a forward step.
+// A context launches its kernels with programmatic stream serialization
+// (QDC_OPT_PDL, on by default): a kernel's CTAs may become resident while
+// its predecessor kernel drains.  Each kernel first waits for the predecessor grid to
+// complete (griddepcontrol.wait -- a no-op when launched without the
+// attribute) and only then touches global memory, then lets its own
+// successor start launching.  This hides the launch and ramp of each of the
+// ~100 kernels of a forward step.
 __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -859,6 +860,77 @@ static __global__ void __launch_bounds__(kThreads) delta_conv_norm_generic(ConvA
         }
         float* dst = conv_dst(a, h, t);
         for (int i = lane; i < width; i += 32) dst[i] = h.group < 2 ? __fmul_rn(conv(i), scale) : conv(i);
+    }
+}
+
+// ------------------------------------------------------ attention out gate
+// out[t][h] = values[b][h][s] * sigmoid(gate[t][h]) (src/backbone.jl:258-259;
+// merge_gate_kernel!, ext/cuda_attention.jl:92-108): the attention output
+// read in its (batch, head, seq, dim) layout, the gate read in place from
+// the packed [q;gate] projection, the token-major result written once.
+
+struct GateArgs {
+    float* out;
+    const float* values;
+    const float* gate;
+    int64_t seq, heads, dim;
+    int64_t v_b, v_h, v_s;   // values strides (elements); unit stride along dim
+    int64_t g_t, g_h;        // gate strides
+    int64_t out_t;           // out token stride; head stride = dim
+    uint32_t units;          // batch * seq * heads
+    FastDiv heads_div, seq_div;
+};
+
+// sigmoid(x) = inv(1 + exp(-x)) with the SFU ops of silu above.
+__device__ __forceinline__ float sigmoid(float x) {
+    return rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(x, -1.4426950408889634f))));
+}
+
+// dim = 128 * CHUNKS: one warp per (token, head), CHUNKS float4 per lane.
+template <int CHUNKS>
+__global__ void __launch_bounds__(kThreads) attn_gate_vec(GateArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    for (uint32_t u = blockIdx.x * warps + (threadIdx.x >> 5); u < a.units; u += gridDim.x * warps) {
+        const uint32_t t = fdiv(u, a.heads_div);
+        const int64_t h = u - t * uint32_t(a.heads);
+        const uint32_t b = fdiv(t, a.seq_div);
+        const int64_t s = t - b * uint32_t(a.seq);
+        const float* v = a.values + int64_t(b) * a.v_b + h * a.v_h + s * a.v_s;
+        const float* g = a.gate + int64_t(t) * a.g_t + h * a.g_h;
+        float* o = a.out + int64_t(t) * a.out_t + h * a.dim;
+        float4 vv[CHUNKS], gg[CHUNKS];
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) {
+            vv[c] = ld_nc_f4(v + (c * 32 + lane) * 4);
+            gg[c] = ld_nc_f4(g + (c * 32 + lane) * 4);
+        }
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) {
+            float4 r;
+            r.x = __fmul_rn(vv[c].x, sigmoid(gg[c].x));
+            r.y = __fmul_rn(vv[c].y, sigmoid(gg[c].y));
+            r.z = __fmul_rn(vv[c].z, sigmoid(gg[c].z));
+            r.w = __fmul_rn(vv[c].w, sigmoid(gg[c].w));
+            st_f4(o + (c * 32 + lane) * 4, r);
+        }
+    }
+}
+
+static __global__ void __launch_bounds__(kThreads) attn_gate_generic(GateArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t units = int64_t(a.units);
+    for (int64_t u = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); u < units;
+         u += int64_t(gridDim.x) * warps) {
+        const int64_t t = u / a.heads, h = u - t * a.heads;
+        const int64_t b = t / a.seq, s = t - b * a.seq;
+        for (int64_t d = lane; d < a.dim; d += 32)
+            a.out[t * a.out_t + h * a.dim + d] =
+                __fmul_rn(__ldg(a.values + b * a.v_b + h * a.v_h + s * a.v_s + d),
+                          sigmoid(__ldg(a.gate + t * a.g_t + h * a.g_h + d)));
     }
 }
 

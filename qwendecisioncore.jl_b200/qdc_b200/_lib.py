@@ -19,6 +19,7 @@ HEADER_PATH = os.path.join(os.path.dirname(_ROOT), "include", "qdc_b200.h")
 
 QDC_OK, QDC_EINVAL, QDC_EBOUNDS, QDC_ECUDA, QDC_ENOMEM, QDC_EDEVICE = range(6)
 QDC_F32, QDC_BF16 = 0, 1
+QDC_OPT_PDL = 1
 
 
 class QdcError(RuntimeError):
@@ -51,6 +52,7 @@ SIGNATURES = {
     "qdc_init": [_int, ctypes.POINTER(_vp)],
     "qdc_destroy": [_vp],
     "qdc_last_error": [_vp],
+    "qdc_set_option": [_vp, _int, _int],
     "qdc_sync": [_vp, _vp],
     "qdc_ws_reserve": [_vp, _sz],
     "qdc_ws_alloc": [_vp, _sz, _sz, ctypes.POINTER(_vp)],
@@ -70,6 +72,8 @@ SIGNATURES = {
     "qdc_q_k_norm_rope": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _i64, _i64,
                           _vp, _vp, _flt, _int, _vp, _vp, _i64, _i64, _i64, _vp],
     "qdc_gated_rms": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _vp],
+    "qdc_attn_gate": [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _i64, _i64, _i64, _i64, _i64, _i64,
+                      _vp],
     "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
                             _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],

@@ -14,7 +14,8 @@ Per layer (native_layer, src/backbone.jl:363-382):
   input norm   -- qdc gather+norm for layer 0, else fused into the previous
                   layer's MLP residual add (qdc_residual_rms)
   attention    -- full: one [q;k;v] GEMM, qdc q/k norm + partial RoPE,
-                  causal GQA attention (torch SDPA), sigmoid gate, o GEMM;
+                  causal GQA attention (torch SDPA), qdc sigmoid gate read
+                  from the attention output in place, o GEMM;
                   delta: one [qkv;z;a;b] GEMM, qdc causal 4-tap conv + SiLU +
                   q/k L2 norms, gates, chunked gated delta rule (torch), qdc
                   gated norm reading z in place, out GEMM
@@ -26,6 +27,8 @@ The projections, attention, conv and delta rule are the reference's
 out-of-scope parts; they run as plain torch Float32 ops (cuBLAS GEMMs with
 TF32 disabled, as the reference computes in Float32, src/backbone.jl:14-16).
 """
+
+import os
 
 import numpy as np
 import torch
@@ -70,6 +73,7 @@ class QwenBackbone:
         self.final_norm = _device_f32(weights["norm.weight"], self.device)
         self.layers = pack_layers(config, weights, self.device)
         self._rope = {}
+        self._graphs = {}  # (B, S, full_mask) -> captured last-token forward
         self.trace = None  # list to record (site, inputs, outputs) of every qdc call
 
     @classmethod
@@ -101,7 +105,7 @@ class QwenBackbone:
 
     # ------------------------------------------------------ attention parts
 
-    def _full_attention(self, layer, y, mask, B, S):
+    def _full_attention(self, layer, y, mask, B, S, full_mask):
         cfg = self.config
         D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
         T = B * S
@@ -120,7 +124,7 @@ class QwenBackbone:
         vh = v.reshape(B, S, Hkv, D).transpose(1, 2)
         # key i visible to query j iff i <= j and mask[i] == 1, else -floatmax
         # (src/backbone.jl:237-242): a fully hidden query averages every key.
-        if bool((mask == 1).all()):
+        if full_mask:
             out = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
         else:
             causal = torch.ones((S, S), dtype=torch.bool, device=self.device).tril()
@@ -128,9 +132,42 @@ class QwenBackbone:
             bias = torch.zeros((B, 1, S, S), dtype=torch.float32, device=self.device)
             bias.masked_fill_(~allowed[:, None], -FLOATMAX32)
             out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=bias, enable_gqa=True)
-        gate = torch.sigmoid(qgate[:, :, D:])
-        out = out.transpose(1, 2).reshape(T, Hq, D) * gate
-        return out.reshape(T, Hq * D) @ layer["out"].t()
+        gated = ops.native_attn_gate(out, qgate[:, :, D:], ctx=self.ctx)
+        self._record("attn_gate", (out, qgate[:, :, D:]), (gated,))
+        return gated @ layer["out"].t()
+
+    def _full_attention_last(self, layer, y, mask, B, S, full_mask):
+        """The final layer's attention for the last query of each sequence
+        only: K/V over the whole context, Q of one token at position S-1
+        (cpu_final_full_attention, src/backbone_cpu.jl:996-1041;
+        last_token_layer, ext/cuda_attention.jl:190-269).  Returns (B, hidden)."""
+        cfg = self.config
+        D, Hq, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+        qw, kw = Hq * 2 * D, Hkv * D
+        y_last = y.view(B, S, -1)[:, S - 1]
+        qgate = (y_last @ layer["qkv"][:qw].t()).view(B, Hq, 2 * D)
+        kv = y @ layer["qkv"][qw:].t()
+        k_raw = kv[:, :kw].view(B * S, Hkv, D)
+        v = kv[:, kw:].view(B * S, Hkv, D)
+        cos, sin = self.rope(S)
+        q = ops.native_qk_norm_rope(qgate[:, :, :D], layer["q_norm"], cfg.eps, cfg.rotary_dim, cos, sin,
+                                    pos_offset=S - 1, seq_len=1, ctx=self.ctx)
+        k = ops.native_qk_norm_rope(k_raw, layer["k_norm"], cfg.eps, cfg.rotary_dim, cos, sin,
+                                    seq_len=S, ctx=self.ctx)
+        self._record("q_norm_rope_last", (qgate[:, :, :D],), (q,))
+        self._record("k_norm_rope", (k_raw,), (k,))
+        qh = q.view(B, 1, Hq, D).transpose(1, 2)
+        kh = k.view(B, S, Hkv, D).transpose(1, 2)
+        vh = v.reshape(B, S, Hkv, D).transpose(1, 2)
+        if full_mask:  # the last query sees every key
+            out = F.scaled_dot_product_attention(qh, kh, vh, enable_gqa=True)
+        else:
+            bias = torch.zeros((B, 1, 1, S), dtype=torch.float32, device=self.device)
+            bias.masked_fill_(mask.view(B, 1, 1, S) != 1, -FLOATMAX32)
+            out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=bias, enable_gqa=True)
+        gated = ops.native_attn_gate(out, qgate[:, :, D:], ctx=self.ctx)
+        self._record("attn_gate", (out, qgate[:, :, D:]), (gated,))
+        return gated @ layer["out"].t()
 
     def _delta_attention(self, layer, y, mask, B, S):
         cfg = self.config
@@ -159,9 +196,14 @@ class QwenBackbone:
 
     # -------------------------------------------------------------- forward
 
-    def _forward(self, ids, mask, B, S):
-        """Final-normalized states (B*S, hidden) on the device.  ids: host
-        int array (B*S,), mask: device int tensor (B*S,)."""
+    def _forward(self, ids, mask, B, S, full_mask, last_only=False):
+        """Final-normalized states on the device: (B*S, hidden), or (B, hidden)
+        for the last token of each sequence when `last_only` (the last-token
+        forward of src/backbone.jl:390-396; its final full-attention layer runs
+        one query and its MLP one token, as ext/cuda_workspace.jl:279-297
+        does).  ids: host int32 array or int32 device tensor (B*S,); mask:
+        int device tensor (B*S,); full_mask: whether every mask value is 1
+        (known on the host, so nothing here waits on the device)."""
         cfg = self.config
         prev_tf32 = torch.backends.cuda.matmul.allow_tf32
         torch.backends.cuda.matmul.allow_tf32 = False
@@ -170,29 +212,38 @@ class QwenBackbone:
             x, y = ops.native_gather_rms(self.embedding, ids, layers[0]["input_norm"], cfg.eps,
                                          ctx=self.ctx)
             self._record("gather_rms", (), (x, y))
+            I = cfg.intermediate
             for i, layer in enumerate(layers):
-                if layer["kind"] == "full":
-                    mixed = self._full_attention(layer, y, mask, B, S)
+                last = i + 1 == len(layers)
+                if last and last_only:
+                    rows = lambda t: t.view(B, S, -1)[:, S - 1]  # the last token of each sequence
+                    if layer["kind"] == "full":
+                        mixed = self._full_attention_last(layer, y, mask, B, S, full_mask)
+                    else:
+                        mixed = rows(self._delta_attention(layer, y, mask, B, S))
+                    x = rows(x)
+                elif layer["kind"] == "full":
+                    mixed = self._full_attention(layer, y, mask, B, S, full_mask)
                 else:
                     mixed = self._delta_attention(layer, y, mask, B, S)
                 r, y = ops.native_residual_rms(x, mixed, layer["post_norm"], cfg.eps, ctx=self.ctx)
                 self._record("post_rms", (x, mixed), (r, y))
                 gu = y @ layer["gate_up"].t()
-                I = cfg.intermediate
                 h, _ = ops.native_mlp_gate(gu[:, :I], gu[:, I:], ctx=self.ctx)
                 self._record("swiglu", (gu[:, :I], gu[:, I:]), (h,))
                 mlp = h @ layer["down"].t()
-                nxt = layers[i + 1]["input_norm"] if i + 1 < len(layers) else self.final_norm
+                nxt = self.final_norm if last else layers[i + 1]["input_norm"]
                 r_in = r.clone() if self.trace is not None else None
                 x, y = ops.native_residual_add_rms(r, mlp, nxt, cfg.eps, ctx=self.ctx)
-                self._record("mlp_rms" if i + 1 < len(layers) else "final_rms", (r_in, mlp), (x, y))
+                self._record("final_rms" if last else "mlp_rms", (r_in, mlp), (x, y))
             return y
         finally:
             torch.backends.cuda.matmul.allow_tf32 = prev_tf32
 
-    def batch_hidden(self, ids, mask=None):
-        """Final-normalized states of B equal-length sequences, (B*S, hidden)
-        on the device.  ids / mask: (B, S) host arrays (mask default ones)."""
+    def batch_hidden(self, ids, mask=None, last_only=False):
+        """Final-normalized states of B equal-length sequences on the device:
+        (B*S, hidden), or (B, hidden) for each sequence's last token.
+        ids / mask: (B, S) host arrays (mask default ones)."""
         ids = np.asarray(ids)
         if ids.ndim != 2:
             raise ArgumentError(1, "batch_hidden takes (batch, sequence) ids")
@@ -203,9 +254,78 @@ class QwenBackbone:
         check_sequence(self.config.vocab, ids.reshape(-1), mask.reshape(-1))
         dmask = torch.from_numpy(mask.reshape(-1).astype(np.int32)).to(self.device)
         with self.ctx.lock:
-            y = self._forward(ids.reshape(-1).astype(np.int32), dmask, B, S)
+            y = self._forward(ids.reshape(-1).astype(np.int32), dmask, B, S,
+                              bool((mask == 1).all()), last_only)
             self.ctx.sync()
         return y
+
+    def last_hidden_graphed(self, ids, mask):
+        """backbone_last_hidden through a CUDA graph cached per (batch,
+        sequence, full mask): pinned host -> device copy of ids and mask,
+        the forward on device ids, and the device -> pinned host copy of the
+        result, replayed as one graph (ext/cuda_io_graph.jl:31-88).  Returns
+        host (B, hidden).  A shape whose capture fails runs eagerly, as the
+        reference falls back (ext/cuda_workspace.jl:247-252)."""
+        ids = np.asarray(ids)
+        mask = np.asarray(mask)
+        if ids.ndim != 2 or mask.shape != ids.shape:
+            raise ArgumentError(1, "Input IDs and mask must have identical lengths.")
+        check_sequence(self.config.vocab, ids.reshape(-1), mask.reshape(-1))
+        B, S = ids.shape
+        key = (B, S, bool((mask == 1).all()))
+        with self.ctx.lock:
+            g = self._graphs.get(key)
+            if g is None:
+                g = self._graphs[key] = _GraphedLastHidden(self, *key)
+            if g.graph is None:
+                return self.batch_hidden(ids, mask, last_only=True).cpu().numpy()
+            return g(ids, mask)
+
+
+class _GraphedLastHidden:
+    """One captured last-token forward for a fixed (B, S, full_mask)."""
+
+    def __init__(self, model, B, S, full_mask):
+        dev = model.device
+        self.model = model
+        self.ids_host = torch.zeros((B * S,), dtype=torch.int32).pin_memory()
+        self.mask_host = torch.ones((B * S,), dtype=torch.int32).pin_memory()
+        self.ids_dev = torch.zeros((B * S,), dtype=torch.int32, device=dev)
+        self.mask_dev = torch.ones((B * S,), dtype=torch.int32, device=dev)
+        self.out_host = torch.empty((B, model.config.hidden), dtype=torch.float32).pin_memory()
+        self.stream = torch.cuda.Stream(dev)
+        self.graph = None
+        try:
+            with torch.cuda.stream(self.stream):
+                self._body(model, B, S, full_mask)  # warm-up: lazy handles, RoPE tables
+            self.stream.synchronize()
+            # the captured kernels read these tables by address: hold them, as
+            # the model's cache replaces them when a longer sequence arrives
+            self.rope = model.rope(S)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=self.stream):
+                self._body(model, B, S, full_mask)
+            self.graph = graph
+        except RuntimeError:
+            self.graph = None
+            torch.cuda.synchronize(dev)
+
+    def _body(self, model, B, S, full_mask):
+        self.ids_dev.copy_(self.ids_host, non_blocking=True)
+        self.mask_dev.copy_(self.mask_host, non_blocking=True)
+        y = model._forward(self.ids_dev, self.mask_dev, B, S, full_mask, last_only=True)
+        self.out_host.copy_(y, non_blocking=True)
+
+    def __call__(self, ids, mask):
+        self.ids_host.copy_(torch.from_numpy(np.ascontiguousarray(ids.reshape(-1), np.int32)))
+        self.mask_host.copy_(torch.from_numpy(np.ascontiguousarray(mask.reshape(-1), np.int32)))
+        # replay() launches on the current stream: make that the graph's own
+        # stream, the one synchronised before the pinned output is read
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
+        self.stream.synchronize()
+        self.model.ctx.sync(self.stream)
+        return self.out_host.numpy().copy()
 
 
 def backbone_hidden(backbone, ids, mask, positions=None):
@@ -229,9 +349,16 @@ def backbone_hidden(backbone, ids, mask, positions=None):
 
 
 def backbone_last_hidden(backbone, ids, mask):
-    """src/backbone.jl:470-490: the last position's state, host vector."""
-    check_sequence(backbone.config.vocab, np.asarray(ids).reshape(-1), np.asarray(mask).reshape(-1))
-    return backbone_hidden(backbone, ids, mask)[-1]
+    """src/backbone.jl:470-490: the last position's state, host vector, by
+    the last-token forward (one-query final attention layer, one-token final
+    MLP) replayed as a cached CUDA graph; QDC_B200_GRAPH=0 runs it eagerly
+    (the reference's QDC_CUDA_GRAPH switch, ext/cuda_workspace.jl:231)."""
+    ids = np.asarray(ids).reshape(1, -1)
+    mask = np.asarray(mask).reshape(1, -1)
+    check_sequence(backbone.config.vocab, ids.reshape(-1), mask.reshape(-1))
+    if os.environ.get("QDC_B200_GRAPH", "1") == "0":
+        return backbone.batch_hidden(ids, mask, last_only=True).cpu().numpy()[0]
+    return backbone.last_hidden_graphed(ids, mask)[0]
 
 
 def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK):

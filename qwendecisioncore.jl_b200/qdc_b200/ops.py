@@ -13,6 +13,8 @@ for CuArrays and the work done by the library's sm_100a kernels:
                        src/backbone.jl:206-235 (CPU form src/backbone_cpu.jl:113-136)
   native_q_k_norm_rope the same for the query and key heads in one launch
   native_gated_rms     src/backbone.jl:339-341, ext/cuda_delta.jl:99-116
+  native_attn_gate     values .* sigmoid(gate), src/backbone.jl:258-259,
+                       ext/cuda_attention.jl:92-108
   native_delta_conv_norm  conv + SiLU + q/k L2 norms of delta_attention,
                        src/backbone.jl:287-314, ext/cuda_delta.jl:8-40,122-146
   native_mlp_gate      src/backbone.jl:352-355, ext/cuda_mlp.jl:49-61
@@ -50,6 +52,18 @@ class Context:
         check(self.lib.qdc_init(self.device.index or 0, ctypes.byref(handle)))
         self.handle = handle
         self.lock = threading.RLock()
+        self._pdl = True
+
+    @property
+    def pdl(self):
+        """Programmatic dependent launch of this context's kernels (on by
+        default; QDC_OPT_PDL of include/qdc_b200.h)."""
+        return self._pdl
+
+    @pdl.setter
+    def pdl(self, on):
+        check(self.lib.qdc_set_option(self.handle, _lib.QDC_OPT_PDL, int(bool(on))), self.handle)
+        self._pdl = bool(on)
 
     def close(self):
         if self.handle:
@@ -422,6 +436,34 @@ def native_gated_rms(o, z, weight, eps, *, out=None, ctx=None, stream=None):
     with ctx.lock:
         check(ctx.lib.qdc_gated_rms(ctx.handle, _ptr(out), _ptr(o), _ptr(z), rows, heads, dim, o_ld,
                                     z_ld, 0, ld_out, _ptr(weight), float(eps), _stream(dev, stream)),
+              ctx.handle)
+    return out
+
+
+def native_attn_gate(values, gate, *, out=None, ctx=None, stream=None):
+    """values * sigmoid(gate) (src/backbone.jl:258-259): values is the
+    attention output (batch, heads, seq, dim) in any strides with unit inner
+    stride; gate (batch*seq, heads, dim) -- e.g. qgate[:, :, dim:] of the
+    packed projection.  Returns (batch*seq, heads*dim)."""
+    dev = _cuda(values, gate, out)
+    if values.dim() != 4 or gate.dim() != 3:
+        raise DimensionMismatch(_lib.QDC_EINVAL, "values (B, H, S, D) and gate (B*S, H, D) expected")
+    B, H, S, D = values.shape
+    if tuple(gate.shape) != (B * S, H, D):
+        raise DimensionMismatch(_lib.QDC_EINVAL, "gate shape differs from the attention output")
+    for t, name in ((values, "values"), (gate, "gate")):
+        if t.dtype != torch.float32:
+            raise ArgumentError(_lib.QDC_EINVAL, f"{name} must be Float32")
+        if t.numel() and D > 1 and t.stride(-1) != 1:
+            raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} needs a unit inner stride")
+    if out is None:
+        out = torch.empty((B * S, H * D), dtype=torch.float32, device=dev)
+    _, _, out_t = _rows(out, "out")
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_attn_gate(ctx.handle, _ptr(out), _ptr(values), _ptr(gate), B, S, H, D,
+                                    values.stride(0), values.stride(1), values.stride(2),
+                                    gate.stride(0), gate.stride(1), out_t, _stream(dev, stream)),
               ctx.handle)
     return out
 

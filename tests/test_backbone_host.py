@@ -47,6 +47,10 @@ def cpu_backbone(monkeypatch, oracle):
         r.copy_(T(rr))
         return r, T(y)
 
+    def qk(x, w, eps, rot, cos, sin, pos_offset=0, seq_len=None, ctx=None, **k):
+        return T(oracle.qk_norm_rope(c(n(x)), n(w), eps, rot, n(cos), n(sin), pos_offset=pos_offset,
+                                     seq_len=seq_len))
+
     def q_k(qi, ki, wq, wk, eps, rot, cos, sin, seq_len=None, ctx=None, **k):
         return (T(oracle.qk_norm_rope(c(n(qi)), n(wq), eps, rot, n(cos), n(sin), seq_len=seq_len)),
                 T(oracle.qk_norm_rope(c(n(ki)), n(wk), eps, rot, n(cos), n(sin), seq_len=seq_len)))
@@ -65,14 +69,18 @@ def cpu_backbone(monkeypatch, oracle):
                                           seq_len=seq_len)
         return T(q), T(kk), T(v)
 
+    def attn_gate(values, gate, ctx=None, **k):
+        return T(oracle.attn_gate(c(n(values)), c(n(gate))))
+
     def rope_table(theta, r, rows, device=None):
         cs, sn = oracle.rope_table(theta, r, rows)
         return T(cs), T(sn)
 
     for name, fn in (("native_gather_rms", gather_rms), ("native_residual_rms", residual_rms),
                      ("native_residual_add_rms", residual_add_rms), ("native_q_k_norm_rope", q_k),
+                     ("native_qk_norm_rope", qk),
                      ("native_gated_rms", gated), ("native_mlp_gate", swiglu),
-                     ("native_delta_conv_norm", conv_norm),
+                     ("native_delta_conv_norm", conv_norm), ("native_attn_gate", attn_gate),
                      ("rope_table", rope_table)):
         monkeypatch.setattr(ops, name, fn)
 
@@ -111,6 +119,23 @@ def test_fixture_forward_orchestration(cpu_backbone, n, holes):
     assert np.all(np.abs(actual - expected) <= 2e-5 + 2e-5 * np.abs(expected))
     assert np.array_equal(qdc_b200.backbone_hidden(model, ids, mask, positions=[1, n]),
                           actual[[0, n - 1]])
+
+
+@pytest.mark.parametrize("n,holes", [(1, False), (9, True), (65, False), (66, True)])
+def test_last_token_forward_orchestration(cpu_backbone, n, holes):
+    """The last-token forward (one-query final attention, one-token final
+    MLP) equals the last row of the all-token forward."""
+    import qdc_b200
+    from qdc_b200.model import load_weights
+    cfg, w = load_weights(GOLDEN)
+    model = cpu_backbone(cfg, w)
+    ids = (np.arange(n) * 7) % 64
+    mask = np.ones(n, np.int64)
+    if holes and n > 1:
+        mask[0:n - 1:3] = 0
+    full = qdc_b200.backbone_hidden(model, ids, mask)[-1]
+    last = model.batch_hidden(ids.reshape(1, -1), mask.reshape(1, -1), last_only=True).numpy()[0]
+    assert np.all(np.abs(last - full) <= 2e-5 + 2e-5 * np.abs(full))
 
 
 def test_chunked_delta_matches_token_recurrence():

@@ -60,6 +60,45 @@ def test_fixture_logits(q, fixture_model, readout, name):
     assert worst <= 1.0
 
 
+def test_last_hidden_graph_replay(q, fixture_model, monkeypatch):
+    """The cached CUDA graph of the last-token forward (test/cuda.jl:17-28,
+    48-65): captured, replayed on changed values at a fixed shape, equal to
+    the eager last-token forward and to the all-token forward's last row."""
+    ids = (np.arange(65) * 5) % 64
+    mask = np.ones(65, np.int64)
+    mask[0:64:3] = 0
+    first = q.backbone_last_hidden(fixture_model, ids, mask)
+    g = fixture_model._graphs[(1, 65, False)]
+    assert g.graph is not None
+    changed = q.backbone_last_hidden(fixture_model, ids[::-1].copy(), mask)
+    assert _violation(changed.astype(np.float64),
+                      q.backbone_hidden(fixture_model, ids[::-1].copy(), mask)[-1]) <= 1.0
+    again = q.backbone_last_hidden(fixture_model, ids, mask)
+    assert np.array_equal(again, first)
+    monkeypatch.setenv("QDC_B200_GRAPH", "0")
+    eager = q.backbone_last_hidden(fixture_model, ids, mask)
+    assert _violation(eager.astype(np.float64), first.astype(np.float64)) <= 1.0
+    assert _violation(first.astype(np.float64), q.backbone_hidden(fixture_model, ids, mask)[-1]) <= 1.0
+
+
+def test_last_hidden_graph_outlives_table_growth(q):
+    """A graph captured at a short length stays right after a longer
+    sequence has replaced the model's cached RoPE tables."""
+    model = q.QwenBackbone.from_directory(GOLDEN, device="cuda")
+    short = (np.arange(9) * 11) % 64
+    mask = np.ones(9, np.int64)
+    mask[0:8:3] = 0
+    first = q.backbone_last_hidden(model, short, mask)
+    long_ids = (np.arange(300) * 7) % 64
+    q.backbone_last_hidden(model, long_ids, np.ones(300, np.int64))
+    torch.cuda.empty_cache()
+    scratch = torch.full((1 << 20,), float("nan"), device="cuda")  # reuse freed blocks
+    again = q.backbone_last_hidden(model, short, mask)
+    del scratch
+    assert np.array_equal(again, first)
+    assert _violation(again.astype(np.float64), q.backbone_hidden(model, short, mask)[-1]) <= 1.0
+
+
 def test_fixture_validation(q, fixture_model):
     # test/backbone.jl:27-33
     for ids, mask in (([1, 2], [1]), ([], []), ([1, 2], [1, 2]), ([64], [1])):
@@ -108,6 +147,17 @@ def test_config1_forward_matches_oracle(q, cfg1_pair, n, holes):
     assert _violation(actual.astype(np.float64), expected.astype(np.float64)) <= 1.0
 
 
+@pytest.mark.parametrize("n", [1, 64, 129])
+def test_config1_last_hidden(q, cfg1_pair, n):
+    from oracle import forward as F
+    model, omodel = cfg1_pair
+    ids = np.random.default_rng(n + 1).integers(0, 4096, n)
+    mask = np.ones(n, np.int64)
+    expected = F.backbone_hidden(omodel, ids, mask)[-1]
+    assert _violation(q.backbone_last_hidden(model, ids, mask).astype(np.float64),
+                      expected.astype(np.float64)) <= 1.0
+
+
 def test_config1_batch_two_by_64(q, cfg1_pair):
     """BASELINE config 1's batch: 2 x 64, full mask, both rows in one pass."""
     from oracle import forward as F
@@ -139,7 +189,7 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
     assert kinds.count("swiglu") == n_layers and kinds.count("gated_rms") == 3
     assert kinds.count("q_norm_rope") == 1 and kinds.count("k_norm_rope") == 1
     assert kinds.count("mlp_rms") == n_layers - 1 and kinds.count("final_rms") == 1
-    assert kinds.count("delta_conv_norm") == 3
+    assert kinds.count("delta_conv_norm") == 3 and kinds.count("attn_gate") == 1
     w = omodel.weights
     cos, sin = oracle.rope_table(cfg.rope_theta, cfg.rotary_dim, 64)
     layer = 0
@@ -169,6 +219,9 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
                                                 cpu(ins[1]).reshape(C, 4), cfg.key_heads, cfg.key_dim,
                                                 cfg.value_heads, cfg.value_dim, seq_len=64)
             assert close(cpu(outs[0]), eq) and close(cpu(outs[1]), ek) and close(cpu(outs[2]), ev)
+        elif site == "attn_gate":
+            ex = oracle.attn_gate(np.ascontiguousarray(cpu(ins[0])), np.ascontiguousarray(cpu(ins[1])))
+            assert close(cpu(outs[0]), ex), site
         elif site == "gated_rms":
             o, z = cpu(ins[0]), np.ascontiguousarray(cpu(ins[1]))
             ex = oracle.gated_rms(o, z, w[p + "linear_attn.norm.weight"], cfg.eps)

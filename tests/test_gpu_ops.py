@@ -407,3 +407,18 @@ def test_delta_conv_norm(q, oracle, tokens, seq_len, kh, kd, vh, vd, pad):
                                           q_out=nan_like((tokens, kh, kd)), k_out=nan_like((tokens, kh, kd)),
                                           v_out=nan_like((tokens, vh, vd)))
     assert f32_close(gq, eq) and f32_close(gk, ek) and f32_close(gv, ev)
+
+
+@pytest.mark.parametrize("B,S,H,D", [(2, 33, 8, 256), (1, 64, 4, 64), (3, 5, 2, 4), (2, 17, 3, 128)])
+def test_attn_gate(q, oracle, B, S, H, D):
+    """values * sigmoid(gate) from an attention output in (B, H, S, D) and
+    the gate half of the packed [q;gate] projection."""
+    r = rng(B * S + H * D)
+    values = r.normal(0, 1, (B, S, H, D)).astype(np.float32)   # stored (B, S, H, D), viewed (B, H, S, D)
+    proj = r.normal(0, 2, (B * S, H, 2 * D)).astype(np.float32)
+    vt = values.transpose(0, 2, 1, 3)
+    expected = oracle.attn_gate(np.ascontiguousarray(vt), np.ascontiguousarray(proj[:, :, D:]))
+    dv = dev(values).transpose(1, 2)
+    dp = dev(proj)
+    got = q.native_attn_gate(dv, dp[:, :, D:], out=nan_like((B * S, H * D)))
+    assert f32_close(got, expected)

@@ -73,9 +73,9 @@ BYTES_PER_TOKEN = (BYTES["gather_rms"] + 18 * BYTES["gated_rms"]
 assert BYTES_PER_TOKEN == 2_392_064
 
 
-# DRAM bytes per token of the dominant kernel (SwiGLU, fp32 out), from the
-# ncu capture summarised in profiles/swiglu_tokens16384.md: dram__bytes_read
-# + dram__bytes_write = 653,557,760 B for 16,384 tokens.  Traffic grows in
+# DRAM bytes per token of the dominant kernel (SwiGLU, fp32 out), from one
+# ncu --set full capture of `bench.py --kernel swiglu --tokens 16384`:
+# dram__bytes_read + dram__bytes_write = 653,557,760 B for 16,384 tokens.  Traffic grows in
 # proportion to the tokens (a pure stream), so a full launch's traffic is
 # this times its tokens.
 SWIGLU_DRAM_BYTES_PER_TOKEN = 653_557_760 / 16384
@@ -332,21 +332,50 @@ def single_kernel(name, tokens, device, seed=1):
         return (lambda: q.native_delta_conv_norm(proj, conv, HK, DK, HV, DV, seq_len=SEQ, q_out=qo,
                                                  k_out=ko, v_out=vo, ctx=ctx),
                 2 * T * QKV_W * 4 + QKV_W * 16)
+    if name == "attn_gate":
+        # the attention output (B, H, S, D) of B = tokens / SEQ sequences and
+        # the gate half of the packed [q;gate] projection
+        nseq = max(T // SEQ, 1)
+        values = normal((nseq, HQ, T // nseq, HEAD_DIM))
+        qgate = normal((nseq * (T // nseq), HQ, 2 * HEAD_DIM))
+        out = torch.empty((qgate.shape[0], HQ * HEAD_DIM), **f)
+        return (lambda: q.native_attn_gate(values, qgate[:, :, HEAD_DIM:], out=out, ctx=ctx),
+                3 * out.numel() * 4)
+    if name == "delta_gates":
+        # a, b at the tail of the packed DeltaNet projection rows; the 2 x HV
+        # columns of a row share one 128-byte line
+        proj = normal((T, PROJ_W))
+        a_decay = normal((HV,)).exp_().neg_()
+        dt_bias = normal((HV,))
+        beta = torch.empty((T, HV), **f)
+        decay = torch.empty((T, HV), **f)
+        return (lambda: q.native_delta_gates(proj, Z_OFF + HV * DV, HV, a_decay, dt_bias, beta=beta,
+                                             decay=decay, ctx=ctx),
+                4 * T * HV * 4)
     raise SystemExit(f"unknown kernel {name}")
 
 
 def time_launches(fn, device, reps, warmup=3):
-    """Average device time (us) of `reps` back-to-back launches."""
+    """Average device time (us) of `reps` back-to-back launches, replayed as
+    one captured CUDA graph so that the host's per-call cost (argument
+    checks, ctypes) cannot leave the GPU idle between short launches."""
     import torch
     for _ in range(warmup):
         fn()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.Stream(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(reps):
+            fn()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()  # warm: first replay uploads the graph
+        s.record()
+        graph.replay()
+        e.record()
     torch.cuda.synchronize(device)
-    s.record()
-    for _ in range(reps):
-        fn()
-    e.record()
-    torch.cuda.synchronize(device)
+    del graph
     return s.elapsed_time(e) * 1e3 / reps
 
 
@@ -358,8 +387,10 @@ CONFIG_CASES = [  # (report name, kernel, tokens)
     ("cfg4_swiglu_f32", "swiglu", 32768),
     ("cfg4_swiglu_bf16", "swiglu_bf16", 32768),
     ("cfg4_swiglu_f32_and_bf16", "swiglu_both", 32768),
-    # the DeltaNet prologue (conv + SiLU + q/k L2 norms) at config-5 shapes
+    # the DeltaNet prologue (conv + SiLU + q/k L2 norms) and the attention
+    # output gate at config-5 shapes
     ("cfg5_delta_conv_norm", "delta_conv_norm", 32768),
+    ("cfg5_attn_gate", "attn_gate", 16384),
 ]
 
 
@@ -389,7 +420,7 @@ def run_single_kernel(args):
     fn, nbytes = single_kernel(args.kernel, args.tokens, device)
     us = time_launches(fn, device, args.steps, args.warmup)
     gbs = nbytes / (us * 1e-6) / 1e9
-    print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "launches": args.warmup + args.steps,
+    print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "launches": args.warmup + 2 * args.steps,
                       "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "peak": peak,
                       "peak_kind": kind}), flush=True)
@@ -553,7 +584,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel alone (gather_rms[_bf16], post_rms[_bf16], swiglu, "
                          "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope, "
-                         "delta_conv_norm)")
+                         "delta_conv_norm, attn_gate, delta_gates)")
     ap.add_argument("--tokens", type=int, default=16384, help="rows for --kernel")
     ap.add_argument("--no-forward", action="store_true", help="skip the whole-forward tokens/s leg")
     ap.add_argument("--forward-steps", type=int, default=2)
@@ -753,7 +784,7 @@ def main():
                          "frac": round(dom_achieved / peak, 4),
                          "traffic": round(T * SWIGLU_DRAM_BYTES_PER_TOKEN),
                          "traffic_note": "dram read+write of one ncu capture at 16384 tokens "
-                                         "(profiles/swiglu_tokens16384.md) scaled to this launch's "
+                                         "(bench.py --kernel swiglu --tokens 16384) scaled to this launch's "
                                          "tokens; reads equal the algorithmic reads, writes fall "
                                          "short by output still dirty in L2 at kernel end",
                          "peak_kind": peak_kind,

@@ -6,7 +6,8 @@
  * overrides through Julia multiple dispatch; the hook is cited (file:line
  * inside the QwenDecisionCore.jl project) beside each declaration.  The
  * reference binds its GPU code with CUDA.jl `@cuda` launches; a Julia
- * extension binds this library with `ccall`.
+ * extension binds this library with `ccall`
+ * (qwendecisioncore.jl_b200/julia/QwenDecisionCoreB200Ext.jl).
  *
  * Conventions
  *  - Layouts are the reference's column-major Julia matrices seen row-major:
@@ -237,6 +238,19 @@ QDC_API int qdc_attn_gate(qdc_ctx *ctx, float *out, const float *values,
                           int heads, int dim, int64_t v_b, int64_t v_h,
                           int64_t v_s, int64_t g_t, int64_t g_h, int64_t out_t,
                           void *stream);
+
+/* Gated DeltaNet gates for every (token, value head):
+ *   beta  = inv(1 + exp(-b)),
+ *   decay = a_decay[h] * softplus(a + dt_bias[h]),
+ *   softplus(x) = max(x, 0) + log1p(exp(-|x|))
+ * (src/backbone.jl:292-297, :196-198).  a of token t, head h at
+ * proj[t*ld_proj + start + h], b at proj[t*ld_proj + start + heads + h] (the
+ * packed [qkv | z | a | b] projection rows, ext/cuda_mlp.jl:27); a_decay =
+ * -exp(A_log) per head; beta and decay are dense [tokens][heads].  Replaces
+ * delta_gates_kernel! (ext/cuda_delta.jl:168-181). */
+QDC_API int qdc_delta_gates(qdc_ctx *ctx, float *beta, float *decay, const float *proj,
+                    int64_t ld_proj, int64_t start, const float *a_decay,
+                    const float *dt_bias, int64_t tokens, int heads, void *stream);
 
 /* DeltaNet prologue in one pass over the packed projection: 4-tap causal
  * depthwise conv + SiLU on the [q | k | v] channels at the start of each

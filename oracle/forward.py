@@ -171,15 +171,6 @@ def _linear(W, x):
     return np.asarray(x, np.float64) @ np.asarray(W, np.float64).T
 
 
-def _sigmoid(x):
-    return 1.0 / (1.0 + np.exp(-x))
-
-
-def _softplus(x):
-    # max(x, 0) + log1p(exp(-|x|)), src/backbone.jl:198
-    return np.maximum(x, 0.0) + np.log1p(np.exp(-np.abs(x)))
-
-
 def full_attention(w, p, x, mask, cfg, trace=None):
     """src/backbone.jl:224-262 with the CPU q/k norm + RoPE of
     src/backbone_cpu.jl:113-136 (tables :90-105) through the oracle."""
@@ -233,10 +224,17 @@ def delta_attention(w, p, x, mask, cfg, trace=None):
     q, k, v = q.astype(np.float64), k.astype(np.float64), v.astype(np.float64)
     z = _linear(w[p + "linear_attn.in_proj_z.weight"], masked).astype(np.float32)
     z = z.reshape(T, cfg.value_heads, cfg.value_dim)
-    beta = _sigmoid(_linear(w[p + "linear_attn.in_proj_b.weight"], masked))
-    a_decay = -np.exp(w[p + "linear_attn.A_log"].astype(np.float64))
-    decay = a_decay * _softplus(_linear(w[p + "linear_attn.in_proj_a.weight"], masked)
-                                + w[p + "linear_attn.dt_bias"].astype(np.float64))
+    # beta = sigmoid(b), decay = a_decay * softplus(a + dt_bias) through the
+    # oracle on Float32 projections (src/backbone.jl:292-297); a_decay =
+    # -1 * exp(A_log) in Float32 (src/backbone.jl:162)
+    ab = np.concatenate([_linear(w[p + "linear_attn.in_proj_a.weight"], masked),
+                         _linear(w[p + "linear_attn.in_proj_b.weight"], masked)], axis=1)
+    ab = ab.astype(np.float32)
+    a_decay = -np.exp(w[p + "linear_attn.A_log"].astype(np.float32))
+    beta, decay = O.delta_gates(ab, 0, cfg.value_heads, a_decay, w[p + "linear_attn.dt_bias"])
+    if trace is not None:
+        trace.append(("delta_gates", p, ab, (beta, decay)))
+    beta, decay = beta.astype(np.float64), decay.astype(np.float64)
     groups = cfg.value_heads // cfg.key_heads
     result = np.empty((T, cfg.value_heads, cfg.value_dim))
     for h in range(cfg.value_heads):

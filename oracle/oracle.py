@@ -52,6 +52,7 @@ _SIGNATURES = {
     "qdo_swiglu": (None, [_f32p, _u16p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64]),
     "qdo_attn_gate": (None, [_f32p, _f32p, _f32p, _i64, _i64, _int, _int, _i64, _i64, _i64, _i64,
                              _i64, _i64]),
+    "qdo_delta_gates": (None, [_f32p, _f32p, _f32p, _i64, _i64, _f32p, _f32p, _i64, _int]),
     "qdo_delta_conv_norm": (None, [_f32p, _f32p, _f32p, _f32p, _i64, _f32p, _i64, _i64, _int,
                                    _int, _int, _int, _flt]),
 }
@@ -299,6 +300,24 @@ def attn_gate(values, gate):
                             H, D, st[0], st[1], st[2], gate.strides[0] // 4, gate.strides[1] // 4,
                             H * D)
     return out
+
+
+def delta_gates(proj, start, heads, a_decay, dt_bias):
+    """proj (tokens, >= start + 2 heads) float32 with unit inner stride.
+    Returns (beta, decay), each (tokens, heads): sigmoid(b) and
+    a_decay * softplus(a + dt_bias), src/backbone.jl:292-297."""
+    assert proj.dtype == np.float32 and proj.ndim == 2
+    assert proj.size == 0 or proj.strides[1] == 4
+    assert start >= 0 and start + 2 * heads <= proj.shape[1]
+    tokens = proj.shape[0] if proj.size else 0
+    a_decay, dt_bias = _f32(a_decay).reshape(-1), _f32(dt_bias).reshape(-1)
+    assert a_decay.size == heads and dt_bias.size == heads
+    beta = np.empty((tokens, heads), np.float32)
+    decay = np.empty((tokens, heads), np.float32)
+    if tokens:
+        lib().qdo_delta_gates(_p(beta), _p(decay), proj.ctypes.data_as(_f32p), proj.strides[0] // 4,
+                              start, _p(a_decay), _p(dt_bias), tokens, heads)
+    return beta, decay
 
 
 def silu(x):

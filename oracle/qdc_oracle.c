@@ -363,6 +363,25 @@ void qdo_attn_gate(float *out, const float *values, const float *gate,
     }
 }
 
+/* ---- DeltaNet gates, src/backbone.jl:292-297 ---------------------------- */
+
+void qdo_delta_gates(float *beta, float *decay, const float *proj, int64_t ld,
+                     int64_t start, const float *a_decay, const float *dt_bias,
+                     int64_t tokens, int heads) {
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
+    for (int64_t t = 0; t < tokens; ++t) {
+        const float *row = proj + t * ld + start;
+        for (int h = 0; h < heads; ++h) {
+            float a = row[h] + dt_bias[h];   /* native_linear(a) .+ dt_bias */
+            float b = row[heads + h];
+            beta[t * heads + h] = 1.0f / (1.0f + expf(-b)); /* native_sigmoid, :196 */
+            /* native_softplus, :198 */
+            float sp = fmaxf(a, 0.0f) + log1pf(expf(-fabsf(a)));
+            decay[t * heads + h] = a_decay[h] * sp;
+        }
+    }
+}
+
 /* ---- SwiGLU, src/backbone.jl:352-355 ------------------------------------ */
 
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,

@@ -140,6 +140,15 @@ void qdo_attn_gate(float *out, const float *values, const float *gate,
                    int64_t v_h, int64_t v_s, int64_t g_t, int64_t g_h,
                    int64_t out_t);
 
+/* Gated DeltaNet gates, src/backbone.jl:292-297 (delta_gates_kernel!,
+ * ext/cuda_delta.jl:168-181): beta = inv(1 + exp(-b)), decay = a_decay *
+ * softplus(a + dt_bias), softplus(x) = max(x, 0) + log1p(exp(-|x|))
+ * (:196-198).  a of token t, head h at proj[t*ld + start + h], b at
+ * proj[t*ld + start + heads + h]; beta, decay dense [tokens][heads]. */
+void qdo_delta_gates(float *beta, float *decay, const float *proj, int64_t ld,
+                     int64_t start, const float *a_decay, const float *dt_bias,
+                     int64_t tokens, int heads);
+
 /* SwiGLU, src/backbone.jl:352-355: h = silu(g) * u; optional fp32 and/or
  * bf16 (src/safetensors.jl:38-42) outputs. */
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,

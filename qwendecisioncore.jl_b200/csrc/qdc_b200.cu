@@ -674,6 +674,34 @@ int qdc_attn_gate(qdc_ctx* ctx, float* out, const float* values, const float* ga
     return launch(ctx, k, grid, a, stream, "attn_gate");
 }
 
+// ----------------------------------------------------------- DeltaNet gates
+
+int qdc_delta_gates(qdc_ctx* ctx, float* beta, float* decay, const float* proj, int64_t ld_proj,
+                    int64_t start, const float* a_decay, const float* dt_bias, int64_t tokens, int heads,
+                    void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (tokens < 0 || heads < 1 || start < 0)
+        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d start=%lld", (long long)tokens, heads,
+                    (long long)start);
+    if (ld_proj < start + 2 * int64_t(heads))
+        return fail(ctx, QDC_EINVAL, "ld_proj %lld < start + 2 heads = %lld", (long long)ld_proj,
+                    (long long)(start + 2 * int64_t(heads)));
+    const int64_t units = tokens * heads;
+    if (units == 0) return QDC_OK;
+    if (!beta || !decay || !proj || !a_decay || !dt_bias)
+        return fail(ctx, QDC_EINVAL, "beta, decay, proj, a_decay and dt_bias are required");
+    if (units >= (int64_t(1) << 32) - (int64_t(1) << 24))
+        return fail(ctx, QDC_EINVAL, "too many (token, head) units");
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    qdc::DeltaGateArgs a{beta, decay, proj, a_decay, dt_bias, ld_proj, start, uint32_t(units), heads,
+                         make_fastdiv(uint32_t(heads))};
+    // one thread per unit: blocks of kThreads threads = kThreads / 32 warps
+    const int64_t warps = (units + 31) / 32;
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(qdc::delta_gates), qdc::kThreads / 32, warps);
+    return launch(ctx, qdc::delta_gates, grid, a, stream, "delta_gates");
+}
+
 // ------------------------------------------------------- DeltaNet prologue
 
 int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj,

@@ -934,6 +934,46 @@ static __global__ void __launch_bounds__(kThreads) attn_gate_generic(GateArgs a)
     }
 }
 
+// ------------------------------------------------------ DeltaNet gates
+// beta = sigmoid(b), decay = a_decay * softplus(a + dt_bias) for every
+// (token, value head) (src/backbone.jl:292-297; delta_gates_kernel!,
+// ext/cuda_delta.jl:168-181), a and b read in place from the packed
+// projection rows: a at columns start..start+heads, b right after.
+
+struct DeltaGateArgs {
+    float* beta;           // [tokens][heads]
+    float* decay;          // [tokens][heads]
+    const float* proj;     // token rows, leading dimension ld
+    const float* a_decay;  // [heads], -exp(A_log)
+    const float* dt_bias;  // [heads]
+    int64_t ld, start;
+    uint32_t units;        // tokens * heads
+    int heads;
+    FastDiv heads_div;
+};
+
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)) (src/backbone.jl:198) with the
+// library's correctly rounded-to-a-few-ulp expf / log1pf.
+__device__ __forceinline__ float softplus(float x) {
+    return __fadd_rn(fmaxf(x, 0.0f), log1pf(expf(-fabsf(x))));
+}
+
+// One thread per (token, head): consecutive threads read consecutive
+// columns of a token's a / b group and write consecutive outputs.
+static __global__ void __launch_bounds__(kThreads) delta_gates(DeltaGateArgs a) {
+    pdl_enter();
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.units; i += stride) {
+        const uint32_t t = fdiv(i, a.heads_div);
+        const int h = int(i - t * uint32_t(a.heads));
+        const float* row = a.proj + int64_t(t) * a.ld + a.start;
+        const float x = __fadd_rn(__ldg(row + h), __ldg(a.dt_bias + h));
+        const float b = __ldg(row + a.heads + h);
+        a.beta[i] = __frcp_rn(__fadd_rn(1.0f, expf(-b)));
+        a.decay[i] = __fmul_rn(__ldg(a.a_decay + h), softplus(x));
+    }
+}
+
 // ---------------------------------------------------------------- SwiGLU
 
 struct SwigluArgs {

@@ -5,15 +5,17 @@
 # every CUDA.jl array, cuBLAS GEMM, attention and DeltaNet path of
 # QwenDecisionCoreCUDAExt and replaces only the per-layer row kernels --
 # gather, RMSNorm (+ residual), q/k norm + partial RoPE, gated RMSNorm,
-# SwiGLU -- by `ccall`s into libqdc_b200.so (include/qdc_b200.h).
+# SwiGLU, the attention output gate, the DeltaNet conv + q/k L2 norms and
+# its beta / decay gates -- by `ccall`s into libqdc_b200.so
+# (include/qdc_b200.h).
 #
 # Selection.  QwenBackbone(dir; device = :cuda) loads CuArrays exactly as
 # before; when the active device is a compute capability 10.0 GPU and the
 # library loads, `use_b200()` is true and the hooks below run the sm_100a
 # kernels.  The CUDA extension's own kernels are not redefined: its
 # `native_*` methods dispatch here through the `B200Kernels` hook table
-# that the maintainer adds to ext/cuda_workspace.jl (see INTEGRATION.md, the
-# five call sites are listed there), so no method is overwritten.
+# that the maintainer adds to ext/cuda_workspace.jl (the call sites are
+# listed in the integration notes), so no method is overwritten.
 #
 # NOTE: Julia is not installed in the environment this library was built
 # and tested in; this file is the binding a maintainer adds, exercised there
@@ -176,6 +178,65 @@ function swiglu!(out::CUDA.CuMatrix{Float32}, packed::CUDA.CuMatrix{Float32})
     return out
 end
 
+"""attn_gate!(merged, values, qgate)  -- merged[:, head, token] =
+values[:, token, head] .* sigmoid(gate of (head, token)), the gate rows
+(head-1)*2dim+dim .+ (1:dim) of the packed [q; gate] projection `qgate`
+(merge_gate_kernel!, ext/cuda_attention.jl:92-108).  `values` is the
+(dim, tokens, heads) attention output; `merged` is (dim*heads, tokens)."""
+function attn_gate!(merged::CUDA.CuMatrix{Float32}, values::CUDA.CuArray{Float32,3},
+                    qgate::CUDA.CuMatrix{Float32})
+    dim, tokens, heads = size(values)
+    ctx = context()
+    check(ccall((:qdc_attn_gate, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Int64, Cint, Cint, Int64,
+                 Int64, Int64, Int64, Int64, Int64, Ptr{Cvoid}),
+                ctx.handle, ptr(merged), ptr(values), ptr(qgate) + dim * sizeof(Float32),
+                Int64(1), Int64(tokens), Cint(heads), Cint(dim), Int64(dim * tokens * heads),
+                Int64(dim * tokens), Int64(dim), Int64(size(qgate, 1)), Int64(2 * dim),
+                Int64(size(merged, 1)), stream_handle()), ctx.handle)
+    return merged
+end
+
+"""delta_gates!(beta, decay, projected, a_decay, dt_bias, start)  -- beta =
+sigmoid(b), decay = a_decay .* softplus(a .+ dt_bias) for the a rows
+start .+ (1:heads) and b rows start+heads .+ (1:heads) of `projected`
+(delta_gates_kernel!, ext/cuda_delta.jl:168-181).  beta and decay are
+(heads, tokens)."""
+function delta_gates!(beta::CUDA.CuMatrix{Float32}, decay::CUDA.CuMatrix{Float32},
+                      projected::CUDA.CuMatrix{Float32}, a_decay, dt_bias, start::Integer)
+    heads, tokens = size(beta)
+    ctx = context()
+    check(ccall((:qdc_delta_gates, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Int64, Ptr{Cvoid}, Ptr{Cvoid},
+                 Int64, Cint, Ptr{Cvoid}),
+                ctx.handle, ptr(beta), ptr(decay), ptr(projected), Int64(size(projected, 1)),
+                Int64(start), ptr(a_decay), ptr(dt_bias), Int64(tokens), Cint(heads),
+                stream_handle()), ctx.handle)
+    return beta, decay
+end
+
+"""delta_conv_norm!(query, key, value, projected, conv, cfg)  -- the causal
+4-tap depthwise conv + SiLU of rows 1:qkv_width of `projected`
+(causal_depthwise_kernel!, ext/cuda_delta.jl:118-146) followed by the q/k
+L2 norms (qk_normalize_kernel!, ext/cuda_delta.jl:8-40) in one pass.
+query, key are (key_dim, key_heads, tokens); value is a dense
+(value_dim, value_heads, tokens) array, read by the delta rule in place of
+rows 2*key_width .+ (1:value_width) of the conv output."""
+function delta_conv_norm!(query::CUDA.CuArray{Float32,3}, key::CUDA.CuArray{Float32,3},
+                          value::CUDA.CuArray{Float32,3}, projected::CUDA.CuMatrix{Float32},
+                          conv::CUDA.CuMatrix{Float32}, cfg)
+    tokens = size(projected, 2)
+    ctx = context()
+    check(ccall((:qdc_delta_conv_norm, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Ptr{Cvoid}, Int64,
+                 Int64, Cint, Cint, Cint, Cint, Cfloat, Ptr{Cvoid}),
+                ctx.handle, ptr(query), ptr(key), ptr(value), ptr(projected),
+                Int64(size(projected, 1)), ptr(conv), Int64(tokens), Int64(0), Cint(cfg.key_heads),
+                Cint(cfg.key_dim), Cint(cfg.value_heads), Cint(cfg.value_dim), 1.0f-6,
+                stream_handle()), ctx.handle)
+    return query, key, value
+end
+
 """sync!() -- the synchronize of native_forward_scope's `finally`
 (ext/cuda_workspace.jl:62-66), reporting device-side id errors."""
 sync!() = check(ccall((:qdc_sync, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}), context().handle,
@@ -189,7 +250,8 @@ function __init__()
         cuda_ext = Base.get_extension(QDC, :QwenDecisionCoreCUDAExt)
         cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!,
                                                           qk_norm_rope!, rope_tables, gated_rms!,
-                                                          swiglu!, sync!))
+                                                          swiglu!, attn_gate!, delta_gates!,
+                                                          delta_conv_norm!, sync!))
     end
 end
 

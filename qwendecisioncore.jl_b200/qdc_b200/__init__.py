@@ -9,8 +9,9 @@ sys.path:  `import qdc_b200`.
 """
 from ._lib import (ArgumentError, DimensionMismatch, QdcError, QDC_BF16, QDC_F32,
                    declared_symbols, load)
-from .ops import (Context, context, native_attn_gate, native_delta_conv_norm, native_gated_rms, native_gather, native_gather_rms,
-                  native_mlp_gate, native_q_k_norm_rope, native_qk_norm_rope, native_residual_add_rms,
+from .ops import (Context, context, native_attn_gate, native_delta_conv_norm, native_delta_gates,
+                  native_gated_rms, native_gather, native_gather_rms, native_mlp_gate,
+                  native_q_k_norm_rope, native_qk_norm_rope, native_residual_add_rms,
                   native_residual_rms, native_rms, rope_table)
 
 from .backbone import QwenBackbone, backbone_hidden, backbone_last_hidden, check_sequence
@@ -19,7 +20,8 @@ from .model import Config
 __all__ = [
     "QwenBackbone", "backbone_hidden", "backbone_last_hidden", "check_sequence", "Config",
     "ArgumentError", "DimensionMismatch", "QdcError", "QDC_BF16", "QDC_F32", "Context", "context",
-    "declared_symbols", "load", "native_attn_gate", "native_delta_conv_norm", "native_gated_rms", "native_gather", "native_gather_rms",
-    "native_mlp_gate", "native_q_k_norm_rope", "native_qk_norm_rope", "native_residual_add_rms", "native_residual_rms",
-    "native_rms", "rope_table",
+    "declared_symbols", "load", "native_attn_gate", "native_delta_conv_norm", "native_delta_gates",
+    "native_gated_rms", "native_gather", "native_gather_rms", "native_mlp_gate",
+    "native_q_k_norm_rope", "native_qk_norm_rope", "native_residual_add_rms",
+    "native_residual_rms", "native_rms", "rope_table",
 ]

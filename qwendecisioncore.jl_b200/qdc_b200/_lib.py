@@ -1,7 +1,7 @@
 """ctypes binding of libqdc_b200.so (the C ABI in include/qdc_b200.h).
 
-This is the Python twin of the `ccall` layer a Julia extension would use
-(INTEGRATION.md shows that binding): plain pointers, sizes and a
+This is the Python twin of the `ccall` layer of the Julia extension
+(qwendecisioncore.jl_b200/julia/QwenDecisionCoreB200Ext.jl): plain pointers, sizes and a
 cudaStream_t, status codes turned into the reference's exception kinds
 (ArgumentError / DimensionMismatch, src/backbone.jl:413-422).
 
@@ -74,6 +74,7 @@ SIGNATURES = {
     "qdc_gated_rms": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _vp],
     "qdc_attn_gate": [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _i64, _i64, _i64, _i64, _i64, _i64,
                       _vp],
+    "qdc_delta_gates": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _vp],
     "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
                             _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],

@@ -17,8 +17,8 @@ Per layer (native_layer, src/backbone.jl:363-382):
                   causal GQA attention (torch SDPA), qdc sigmoid gate read
                   from the attention output in place, o GEMM;
                   delta: one [qkv;z;a;b] GEMM, qdc causal 4-tap conv + SiLU +
-                  q/k L2 norms, gates, chunked gated delta rule (torch), qdc
-                  gated norm reading z in place, out GEMM
+                  q/k L2 norms, qdc beta/decay gates, chunked gated delta
+                  rule (torch), qdc gated norm reading z in place, out GEMM
   post norm    -- qdc residual add + RMSNorm
   MLP          -- one [gate;up] GEMM, qdc SwiGLU, down GEMM
   residual add -- fused with the next layer's input norm / the final norm.
@@ -183,10 +183,13 @@ class QwenBackbone:
         q = q.view(B, S, cfg.key_heads, cfg.key_dim)
         k = k.view(B, S, cfg.key_heads, cfg.key_dim)
         v = v.view(B, S, cfg.value_heads, cfg.value_dim)
-        a = proj[:, C + vw:C + vw + cfg.value_heads].view(B, S, cfg.value_heads)
-        b = proj[:, C + vw + cfg.value_heads:C + vw + 2 * cfg.value_heads].view(B, S, cfg.value_heads)
-        beta = torch.sigmoid(b)
-        decay = layer["a_decay"] * F.softplus(a + layer["dt_bias"])
+        # beta = sigmoid(b), decay = a_decay * softplus(a + dt_bias), a and b
+        # read in place from the projection (src/backbone.jl:292-297)
+        beta, decay = ops.native_delta_gates(proj, C + vw, cfg.value_heads, layer["a_decay"],
+                                             layer["dt_bias"], ctx=self.ctx)
+        self._record("delta_gates", (proj[:, C + vw:C + vw + 2 * cfg.value_heads],), (beta, decay))
+        beta = beta.view(B, S, cfg.value_heads)
+        decay = decay.view(B, S, cfg.value_heads)
         o = chunked_delta(q, k, v, beta, decay, cfg.value_heads // cfg.key_heads)
         o = o.reshape(T, cfg.value_heads, cfg.value_dim)
         z = proj[:, C:C + vw].view(T, cfg.value_heads, cfg.value_dim)

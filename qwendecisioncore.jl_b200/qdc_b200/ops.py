@@ -468,6 +468,36 @@ def native_attn_gate(values, gate, *, out=None, ctx=None, stream=None):
     return out
 
 
+def native_delta_gates(proj, start, heads, a_decay, dt_bias, *, beta=None, decay=None, ctx=None,
+                       stream=None):
+    """beta = sigmoid(b), decay = a_decay * softplus(a + dt_bias) per (token,
+    head) (src/backbone.jl:292-297), a = proj[:, start:start+heads] and b =
+    proj[:, start+heads:start+2*heads] read in place.  Returns dense
+    (tokens, heads) beta and decay."""
+    dev = _cuda(proj, a_decay, dt_bias, beta, decay)
+    if proj.dtype != torch.float32:
+        raise ArgumentError(_lib.QDC_EINVAL, "proj must be Float32")
+    tokens, width, ld = _rows(proj, "proj")
+    if start < 0 or heads < 1 or start + 2 * heads > width:
+        raise DimensionMismatch(_lib.QDC_EINVAL, "a and b columns fall outside proj")
+    for t, name in ((a_decay, "a_decay"), (dt_bias, "dt_bias")):
+        if t.dtype != torch.float32 or t.numel() != heads or (heads > 1 and t.stride(-1) != 1):
+            raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} must be {heads} contiguous Float32 values")
+    outs = []
+    for t, name in ((beta, "beta"), (decay, "decay")):
+        if t is None:
+            t = torch.empty((tokens, heads), dtype=torch.float32, device=dev)
+        elif t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != tokens * heads:
+            raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} must be a dense ({tokens}, {heads}) Float32")
+        outs.append(t)
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_delta_gates(ctx.handle, _ptr(outs[0]), _ptr(outs[1]), _ptr(proj), ld, int(start),
+                                      _ptr(a_decay), _ptr(dt_bias), tokens, int(heads),
+                                      _stream(dev, stream)), ctx.handle)
+    return outs[0], outs[1]
+
+
 def native_delta_conv_norm(proj, conv_w, key_heads, key_dim, value_heads, value_dim, *, seq_len=None,
                            eps=1e-6, q_out=None, k_out=None, v_out=None, ctx=None, stream=None):
     """The Gated DeltaNet's row work after its projection GEMM, in one pass:

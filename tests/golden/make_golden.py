@@ -7,7 +7,7 @@ test/backbone.jl:1-34).  Those files are data, not code: this script copies
 them byte for byte so the parity tests can run where the reference tree is
 absent, and records each file's SHA-256 in MANIFEST.json.
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
 
 `cuda_reference.json` (21 cases x 3 rows, lengths 1-256) sits beside the
 pinned `reference.json` in the reference but no reference test loads it; it
@@ -24,7 +24,9 @@ FILES = ("config.json", "model.safetensors", "readout.safetensors",
 
 
 def main(argv):
-    root = argv[1] if len(argv) > 1 else "/root/reference"
+    if len(argv) != 2:
+        raise SystemExit("usage: make_golden.py REFERENCE_ROOT (the QwenDecisionCore.jl checkout)")
+    root = argv[1]
     src = os.path.join(root, "test", "fixtures", "native")
     dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "native")
     os.makedirs(dst, exist_ok=True)

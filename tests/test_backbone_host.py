@@ -69,6 +69,10 @@ def cpu_backbone(monkeypatch, oracle):
                                           seq_len=seq_len)
         return T(q), T(kk), T(v)
 
+    def delta_gates(proj, start, heads, a_decay, dt_bias, ctx=None, **k):
+        beta, decay = oracle.delta_gates(c(n(proj)), start, heads, n(a_decay), n(dt_bias))
+        return T(beta), T(decay)
+
     def attn_gate(values, gate, ctx=None, **k):
         return T(oracle.attn_gate(c(n(values)), c(n(gate))))
 
@@ -80,7 +84,8 @@ def cpu_backbone(monkeypatch, oracle):
                      ("native_residual_add_rms", residual_add_rms), ("native_q_k_norm_rope", q_k),
                      ("native_qk_norm_rope", qk),
                      ("native_gated_rms", gated), ("native_mlp_gate", swiglu),
-                     ("native_delta_conv_norm", conv_norm), ("native_attn_gate", attn_gate),
+                     ("native_delta_conv_norm", conv_norm), ("native_delta_gates", delta_gates),
+                     ("native_attn_gate", attn_gate),
                      ("rope_table", rope_table)):
         monkeypatch.setattr(ops, name, fn)
 

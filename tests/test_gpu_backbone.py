@@ -190,6 +190,7 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
     assert kinds.count("q_norm_rope") == 1 and kinds.count("k_norm_rope") == 1
     assert kinds.count("mlp_rms") == n_layers - 1 and kinds.count("final_rms") == 1
     assert kinds.count("delta_conv_norm") == 3 and kinds.count("attn_gate") == 1
+    assert kinds.count("delta_gates") == 3
     w = omodel.weights
     cos, sin = oracle.rope_table(cfg.rope_theta, cfg.rotary_dim, 64)
     layer = 0
@@ -219,6 +220,12 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
                                                 cpu(ins[1]).reshape(C, 4), cfg.key_heads, cfg.key_dim,
                                                 cfg.value_heads, cfg.value_dim, seq_len=64)
             assert close(cpu(outs[0]), eq) and close(cpu(outs[1]), ek) and close(cpu(outs[2]), ev)
+        elif site == "delta_gates":
+            H = cfg.value_heads
+            lay = model.layers[layer]
+            eb, ed = oracle.delta_gates(np.ascontiguousarray(cpu(ins[0])), 0, H, cpu(lay["a_decay"]),
+                                        cpu(lay["dt_bias"]))
+            assert close(cpu(outs[0]), eb) and close(cpu(outs[1]), ed), site
         elif site == "attn_gate":
             ex = oracle.attn_gate(np.ascontiguousarray(cpu(ins[0])), np.ascontiguousarray(cpu(ins[1])))
             assert close(cpu(outs[0]), ex), site

@@ -422,3 +422,27 @@ def test_attn_gate(q, oracle, B, S, H, D):
     dp = dev(proj)
     got = q.native_attn_gate(dv, dp[:, :, D:], out=nan_like((B * S, H * D)))
     assert f32_close(got, expected)
+
+
+@pytest.mark.parametrize("tokens,heads,lead,tail", [(4096, 16, 6144 + 2048, 0), (33, 4, 9, 3),
+                                                    (1, 1, 0, 0), (0, 8, 5, 0), (257, 48, 17, 1)])
+def test_delta_gates(q, oracle, tokens, heads, lead, tail):
+    """beta / decay from the a, b columns at the tail of packed projection
+    rows (src/backbone.jl:292-297), including |a + dt_bias| up to ~60."""
+    r = rng(tokens + heads)
+    proj = r.normal(0, 20, (tokens, lead + 2 * heads + tail)).astype(np.float32)
+    a_decay = -np.exp(r.normal(0, 1, heads)).astype(np.float32)
+    dt_bias = r.normal(0, 1, heads).astype(np.float32)
+    eb, ed = oracle.delta_gates(proj, lead, heads, a_decay, dt_bias)
+    gb, gd = q.native_delta_gates(dev(proj), lead, heads, dev(a_decay), dev(dt_bias),
+                                  beta=nan_like((tokens, heads)), decay=nan_like((tokens, heads)))
+    assert f32_close(gb, eb) and f32_close(gd, ed)
+
+
+def test_delta_gates_rejects_bad_columns(q):
+    proj = torch.zeros((4, 10), device="cuda")
+    h = torch.zeros(4, device="cuda")
+    with pytest.raises(q.DimensionMismatch):
+        q.native_delta_gates(proj, 3, 4, h, h)   # 3 + 8 > 10
+    with pytest.raises(q.DimensionMismatch):
+        q.native_delta_gates(proj, 0, 4, h[:3], h)

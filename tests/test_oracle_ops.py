@@ -156,6 +156,29 @@ def test_swiglu_and_silu_edges(oracle):
     assert np.isnan(oracle.silu(np.array([-np.inf], np.float32)))[0]
 
 
+def test_delta_gates_edges_and_packed_layout(oracle):
+    """beta = inv(1 + exp(-b)), decay = a_decay * (max(x, 0) + log1p(exp(-|x|)))
+    with x = a + dt_bias (src/backbone.jl:196-198, :292-297), a and b read
+    from the tail of packed projection rows."""
+    heads = 5
+    edge = np.array([0.0, 1.0, -1.0, 30.0, -30.0, 100.0, -100.0, 0.5, -0.25, 7.0], np.float32)
+    a = np.stack([edge[(np.arange(heads) + t) % edge.size] for t in range(6)])
+    b = -a[:, ::-1].copy()
+    lead = 9
+    proj = np.concatenate([ramp(6 * lead).reshape(6, lead), a, b, np.ones((6, 3), np.float32)], axis=1)
+    proj = proj.astype(np.float32)
+    a_decay = -np.exp(ramp(heads, np.cos)).astype(np.float32)
+    dt_bias = (0.1 * ramp(heads)).astype(np.float32)
+    beta, decay = oracle.delta_gates(proj, lead, heads, a_decay, dt_bias)
+    x = a.astype(np.float64) + dt_bias.astype(np.float64)
+    sp = np.maximum(x, 0.0) + np.log1p(np.exp(-np.abs(x)))
+    assert close(beta, 1.0 / (1.0 + np.exp(-b.astype(np.float64))))
+    assert close(decay, a_decay.astype(np.float64) * sp)
+    assert beta.shape == decay.shape == (6, heads)
+    empty = oracle.delta_gates(proj[:0], lead, heads, a_decay, dt_bias)
+    assert empty[0].shape == (0, heads)
+
+
 def test_swiglu_packed_layout(oracle):
     rows, width = 5, 16
     packed = ramp(rows * 2 * width).reshape(rows, 2 * width)

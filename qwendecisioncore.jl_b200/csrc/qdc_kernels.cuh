@@ -246,6 +246,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
     constexpr int N = C::N;
     constexpr int W = 32 * N * CHUNKS;
     __shared__ __align__(16) float gterm[W];
+    pdl_enter();
     if (a.gamma) {  // gamma is NULL for a plain gather (no y output)
         for (int i = threadIdx.x; i < W; i += blockDim.x)
             gterm[i] = a.centered ? __fadd_rn(1.0f, a.gamma[i]) : a.gamma[i];

@@ -446,3 +446,27 @@ def test_delta_gates_rejects_bad_columns(q):
         q.native_delta_gates(proj, 3, 4, h, h)   # 3 + 8 > 10
     with pytest.raises(q.DimensionMismatch):
         q.native_delta_gates(proj, 0, 4, h[:3], h)
+
+
+@pytest.mark.parametrize("width_heads", [16, 8])
+def test_row_kernel_waits_for_its_producer(q, oracle, width_heads):
+    """Kernels launch with programmatic dependent launch: a residual norm
+    issued right behind the gated norm that writes its input (a NaN-filled
+    buffer) must read the finished rows, never the fill."""
+    T, H, D = 16384, width_heads, 128
+    r = rng(T + H)
+    o = r.normal(0, 1, (T, H, D)).astype(np.float32)
+    z = r.normal(0, 1, (T, H, D)).astype(np.float32)
+    wg = (1 + r.normal(0, 0.02, D)).astype(np.float32)
+    m = r.normal(0, 1, (T, H * D)).astype(np.float32)
+    wr = r.normal(0, 0.02, H * D).astype(np.float32)
+    gated = oracle.gated_rms(o, z, wg, 1e-6)
+    ex_r, ex_y = oracle.residual_rms(gated, m, wr, 1e-6)
+    do, dz, dwg, dm, dwr = dev(o), dev(z), dev(wg), dev(m), dev(wr)
+    for _ in range(3):
+        g = nan_like((T, H * D))
+        q.native_gated_rms(do, dz, dwg, 1e-6, out=g)
+        rr, yy = q.native_residual_rms(g, dm, dwr, 1e-6, out_r=nan_like((T, H * D)),
+                                       out_y=nan_like((T, H * D)))
+        assert not torch.isnan(yy).any()
+        assert f32_close(rr, ex_r) and f32_close(yy, ex_y)

@@ -726,8 +726,8 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
         make_fastdiv(uint32_t(period < (int64_t(1) << 31) ? period : (int64_t(1) << 31)));
     const bool aligned = aligned16(proj) && ld_proj % 4 == 0 && aligned16(conv_w) && aligned16(q_out) &&
                          aligned16(k_out) && aligned16(v_out) && tokens < (int64_t(1) << 31);
-    // Shared-memory pipeline: 32-token x 4-head tiles, 3 stages (210 KB).
-    constexpr int PR = 32, PS = 3;
+    // Shared-memory pipeline: 48-token x 4-head tiles, 2 stages (204 KB).
+    constexpr int PR = 48, PS = 2;
     const int64_t groups = per_tok / 4;
     const int64_t tiles = (tokens + PR - 1) / PR * groups;
     if (aligned && key_dim == 128 && value_dim == 128 && per_tok % 4 == 0 &&

@@ -396,6 +396,9 @@ def test_c_abi_rejects_bad_arguments_before_launch(q):
     (9, 3, 1, 2, 2, 2, 7),             # fixture dims, generic path
     (50, 25, 2, 64, 3, 96, 4),         # generic head widths
     (1, 0, 2, 128, 4, 128, 8),
+    (48, 7, 2, 128, 4, 128, 0),        # exactly one pipeline tile, short sequences
+    (49, 0, 16, 128, 16, 128, 0),      # one token past a tile
+    (4100, 2048, 4, 128, 8, 128, 32),  # sequence starts inside tiles (2048 = 42 x 48 + 32)
 ])
 def test_delta_conv_norm(q, oracle, tokens, seq_len, kh, kd, vh, vd, pad):
     r = rng(tokens + kd + vd)

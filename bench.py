@@ -355,19 +355,32 @@ def single_kernel(name, tokens, device, seed=1):
     raise SystemExit(f"unknown kernel {name}")
 
 
-def time_launches(fn, device, reps, warmup=3):
-    """Average device time (us) of `reps` back-to-back launches, replayed as
-    one captured CUDA graph so that the host's per-call cost (argument
-    checks, ctypes) cannot leave the GPU idle between short launches."""
+L2_BYTES = 126 * 2 ** 20
+
+
+def kernel_sets(name, tokens, device, max_sets=8):
+    """Launch functions of `name` on independent input/output sets, enough of
+    them (up to `max_sets`) that consecutive launches touch >= 3 x L2 before
+    a set is reused; returns (functions, algorithmic bytes per launch)."""
+    fn, nbytes = single_kernel(name, tokens, device, seed=1)
+    sets = min(max_sets, -(-3 * L2_BYTES // nbytes))
+    return [fn] + [single_kernel(name, tokens, device, seed=1 + i)[0] for i in range(1, sets)], nbytes
+
+
+def time_launches(fns, device, reps, warmup=3):
+    """Average device time (us) of `reps` back-to-back launches cycling over
+    the input sets `fns`, replayed as one captured CUDA graph so that the
+    host's per-call cost (argument checks, ctypes) cannot leave the GPU idle
+    between short launches."""
     import torch
-    for _ in range(warmup):
-        fn()
+    for i in range(warmup):
+        fns[i % len(fns)]()
     torch.cuda.synchronize(device)
     stream = torch.cuda.Stream(device)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for _ in range(reps):
-            fn()
+        for i in range(reps):
+            fns[i % len(fns)]()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         graph.replay()  # warm: first replay uploads the graph
@@ -396,17 +409,17 @@ CONFIG_CASES = [  # (report name, kernel, tokens)
 
 def kernel_configs(device, peak, reps=20):
     """BASELINE configs 2-4 as single-kernel workloads: GB/s and fraction of
-    the HBM peak, each averaged over `reps` back-to-back launches on inputs
-    larger than L2."""
+    the HBM peak, each averaged over `reps` back-to-back launches that cycle
+    over independent input sets, >= 3 x L2 touched before a set is reused."""
     import torch
     out = {}
     for label, name, tokens in CONFIG_CASES:
-        fn, nbytes = single_kernel(name, tokens, device)
-        us = time_launches(fn, device, reps)
+        fns, nbytes = kernel_sets(name, tokens, device)
+        us = time_launches(fns, device, reps)
         gbs = nbytes / (us * 1e-6) / 1e9
         out[label] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
-                      "bytes": nbytes}
-        del fn
+                      "bytes": nbytes, "input_sets": len(fns)}
+        del fns
         torch.cuda.empty_cache()
     return out
 
@@ -417,10 +430,11 @@ def run_single_kernel(args):
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     peak, kind = hbm_peak()
-    fn, nbytes = single_kernel(args.kernel, args.tokens, device)
-    us = time_launches(fn, device, args.steps, args.warmup)
+    fns, nbytes = kernel_sets(args.kernel, args.tokens, device)
+    us = time_launches(fns, device, args.steps, args.warmup)
     gbs = nbytes / (us * 1e-6) / 1e9
     print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "launches": args.warmup + 2 * args.steps,
+                      "input_sets": len(fns),
                       "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
                       "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "peak": peak,
                       "peak_kind": kind}), flush=True)

@@ -187,6 +187,7 @@ int launch_rows(qdc_ctx* ctx, const qdc::RowArgs& a, void* stream) {
     constexpr int64_t N = 16 / sizeof(T);
     const int64_t e = sizeof(T);
     bool vec = a.width % (32 * N) == 0 && aligned16(a.x) && aligned16(a.out_y) &&
+               (a.gamma == nullptr || aligned16(a.gamma)) &&
                (a.out_r == nullptr || aligned16(a.out_r)) && (a.m == nullptr || aligned16(a.m)) &&
                (a.ld_x * e) % 16 == 0 && (a.ld_y * e) % 16 == 0 &&
                (a.out_r == nullptr || (a.ld_r * e) % 16 == 0) &&
@@ -580,8 +581,9 @@ int qk_impl(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const f
     const int half = rotary / 2;
     const int64_t units = tokens * (q_heads + k_heads);
     bool vec = aligned16(q_out) && aligned16(q_in) && q_tok % 4 == 0 && q_head % 4 == 0 &&
+               aligned16(q_gamma) &&
                (k_heads == 0 || (aligned16(k_out) && aligned16(k_in) && k_tok % 4 == 0 &&
-                                 k_head % 4 == 0)) &&
+                                 k_head % 4 == 0 && aligned16(k_gamma))) &&
                (rotary == 0 || (half % 4 == 0 && aligned16(cos_tab) && aligned16(sin_tab)));
     // The vector kernel counts units and positions in 32 bits.
     vec = vec && units < (int64_t(1) << 32) - (int64_t(1) << 24);
@@ -629,8 +631,8 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
     const int64_t row_width = int64_t(heads) * dim;
     if (o_ld < row_width || out_ld < row_width || z_off < 0 || z_ld < z_off + row_width)
         return fail(ctx, QDC_EINVAL, "leading dimensions too small for heads*dim=%lld", (long long)row_width);
-    bool vec = aligned16(out) && aligned16(o) && aligned16(z) && o_ld % 4 == 0 && z_ld % 4 == 0 &&
-               z_off % 4 == 0 && out_ld % 4 == 0;
+    bool vec = aligned16(out) && aligned16(o) && aligned16(z) && aligned16(gamma) && o_ld % 4 == 0 &&
+               z_ld % 4 == 0 && z_off % 4 == 0 && out_ld % 4 == 0;
     vec = vec && rows * heads < (int64_t(1) << 32) - (int64_t(1) << 24);
     qdc::HeadArgs a{out, nullptr, o, nullptr, z, gamma, nullptr, nullptr, nullptr, eps, heads, 0, dim,
                     0, rows * heads, o_ld, dim, 0, 0, z_ld, z_off, out_ld, 0, 0, 0,

@@ -10,7 +10,9 @@
 //  * the row lives in registers between the reduction and the write-back,
 //    so x (and m) are read exactly once -- the reference CUDA kernels read
 //    them twice (ext/cuda_workspace.jl:139-194);
-//  * gamma (and 1+gamma) is staged once per CTA in shared memory;
+//  * gamma (and 1+gamma) is read through L1 at its point of use, not staged
+//    in shared memory behind a block barrier, so a kernel's first row loads
+//    issue right after it starts (the kernel boundaries of a short step);
 //  * reductions are warp shuffles; RoPE partners are exchanged by shuffle
 //    instead of being re-read from global (ext/cuda_attention.jl:35);
 //  * Float32 arithmetic uses explicitly rounded intrinsics (__fmul_rn,
@@ -245,13 +247,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
     using C = Chunk<T>;
     constexpr int N = C::N;
     constexpr int W = 32 * N * CHUNKS;
-    __shared__ __align__(16) float gterm[W];
     pdl_enter();
-    if (a.gamma) {  // gamma is NULL for a plain gather (no y output)
-        for (int i = threadIdx.x; i < W; i += blockDim.x)
-            gterm[i] = a.centered ? __fadd_rn(1.0f, a.gamma[i]) : a.gamma[i];
-    }
-    __syncthreads();
 
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
@@ -308,7 +304,16 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
                 T* yr = static_cast<T*>(a.out_y) + row * a.ld_y;
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c) {
-                    const float* g = gterm + (c * 32 + lane) * N;
+                    float g[N];
+#pragma unroll
+                    for (int q = 0; q < N; q += 4) {
+                        const float4 g4 = __ldg(reinterpret_cast<const float4*>(a.gamma + (c * 32 + lane) * N + q));
+                        g[q] = g4.x; g[q + 1] = g4.y; g[q + 2] = g4.z; g[q + 3] = g4.w;
+                    }
+                    if (a.centered) {
+#pragma unroll
+                        for (int q = 0; q < N; ++q) g[q] = __fadd_rn(1.0f, g[q]);
+                    }
 #pragma unroll
                     for (int j = 0; j < N; ++j)
                         v[c][j] = bad[k] ? v[c][j] : __fmul_rn(__fmul_rn(v[c][j], scale), g[j]);
@@ -419,12 +424,6 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
     pdl_enter();
     constexpr int D = 4 * LPU * CHUNKS;
     constexpr int UPW = 32 / LPU;
-    __shared__ __align__(16) float gterm[2][D];
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        gterm[0][i] = GATED ? a.gamma[i] : __fadd_rn(1.0f, a.gamma[i]);
-        if (!GATED && a.heads2 > 0) gterm[1][i] = __fadd_rn(1.0f, a.gamma2[i]);
-    }
-    __syncthreads();
 
     const int lane = threadIdx.x & 31;
     const int seg = lane / LPU;
@@ -483,10 +482,14 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
             }
             s = segment_sum<LPU>(s);
             const float scale = rms_scale(s, 1.0f / float(D), a.eps);
-            const float* gt = gterm[GATED ? 0 : un[k].group];
+            const float* gt = (GATED || un[k].group == 0) ? a.gamma : a.gamma2;
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c) {
-                const float4 g = *reinterpret_cast<const float4*>(gt + (c * LPU + l) * 4);
+                float4 g = __ldg(reinterpret_cast<const float4*>(gt + (c * LPU + l) * 4));
+                if (!GATED) {
+                    g.x = __fadd_rn(1.0f, g.x); g.y = __fadd_rn(1.0f, g.y);
+                    g.z = __fadd_rn(1.0f, g.z); g.w = __fadd_rn(1.0f, g.w);
+                }
                 float4& x = v[k][c];
                 x.x = __fmul_rn(__fmul_rn(x.x, scale), g.x);
                 x.y = __fmul_rn(__fmul_rn(x.y, scale), g.y);

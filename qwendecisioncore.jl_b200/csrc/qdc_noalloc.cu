@@ -138,7 +138,7 @@ extern "C" int qdc_gather_rms_noalloc(void* out_x, void* out_y, const void* tabl
                    n, hidden, hidden, hidden, hidden, hidden, vocab};
     const int64_t esz = dtype == QDC_F32 ? 4 : 2;
     const bool vec = aligned16(table) && aligned16(out_x) && aligned16(out_y) && aligned16(add) &&
-                     (hidden * esz) % 16 == 0;
+                     aligned16(gamma) && (hidden * esz) % 16 == 0;
     void (*k)(qdc::RowArgs) = dtype == QDC_F32 ? pick_kernel<float>(hidden, vec)
                                                : pick_kernel<uint16_t>(hidden, vec);
     int per_sm = 1;

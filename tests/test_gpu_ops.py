@@ -473,3 +473,44 @@ def test_row_kernel_waits_for_its_producer(q, oracle, width_heads):
                                        out_y=nan_like((T, H * D)))
         assert not torch.isnan(yy).any()
         assert f32_close(rr, ex_r) and f32_close(yy, ex_y)
+
+
+def _misaligned(a):
+    """A device copy of float32 `a` that starts 4 bytes past a 16-byte
+    boundary (the vector kernels read gamma as float4; the host must route
+    such a gamma to the scalar kernels)."""
+    a = np.ascontiguousarray(a, np.float32)
+    buf = torch.empty(a.size + 4, dtype=torch.float32, device="cuda")
+    view = buf[1:1 + a.size]
+    view.copy_(torch.from_numpy(a))
+    assert view.data_ptr() % 16 == 4
+    return view
+
+
+def test_misaligned_gamma_takes_scalar_kernels(q, oracle):
+    r = rng(5)
+    x = r.normal(0, 1, (37, 1024)).astype(np.float32)
+    m = r.normal(0, 1, (37, 1024)).astype(np.float32)
+    w = r.normal(0, 0.02, 1024).astype(np.float32)
+    er, ey = oracle.residual_rms(x, m, w, 1e-6)
+    rr, yy = q.native_residual_rms(dev(x), dev(m), _misaligned(w), 1e-6)
+    assert f32_close(rr, er) and f32_close(yy, ey)
+    table = r.normal(0, 0.02, (500, 1024)).astype(np.float32)
+    ids = r.integers(0, 500, 37).astype(np.int32)
+    ex, ey = oracle.gather_rms(table, ids, m, w, 1e-6)
+    gx, gy = q.native_gather_rms(dev(table), ids, _misaligned(w), 1e-6, add=dev(m))
+    assert np.array_equal(gx.cpu().numpy(), ex) and f32_close(gy, ey)
+    o = r.normal(0, 1, (37, 4, 128)).astype(np.float32)
+    z = r.normal(0, 1, (37, 4, 128)).astype(np.float32)
+    wg = (1 + r.normal(0, 0.02, 128)).astype(np.float32)
+    assert f32_close(q.native_gated_rms(dev(o), dev(z), _misaligned(wg), 1e-6),
+                     oracle.gated_rms(o, z, wg, 1e-6))
+    qi = r.normal(0, 1, (37, 8, 256)).astype(np.float32)
+    ki = r.normal(0, 1, (37, 2, 256)).astype(np.float32)
+    wq = r.normal(0, 0.02, 256).astype(np.float32)
+    wk = r.normal(0, 0.02, 256).astype(np.float32)
+    cos, sin = oracle.rope_table(1e7, 64, 37)
+    dc, ds = q.rope_table(1e7, 64, 37, device="cuda")
+    gq, gk = q.native_q_k_norm_rope(dev(qi), dev(ki), _misaligned(wq), dev(wk), 1e-6, 64, dc, ds)
+    assert f32_close(gq, oracle.qk_norm_rope(qi, wq, 1e-6, 64, cos, sin))
+    assert f32_close(gk, oracle.qk_norm_rope(ki, wk, 1e-6, 64, cos, sin))

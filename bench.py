@@ -44,6 +44,7 @@ for _p in (ROOT, PKG):
 
 METRIC = "fused layer-kernel HBM GB/s (% of roofline) and forward tokens/sec at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+SPEC_HBM_GBS = 8000.0  # B200 HBM3e data-sheet bandwidth (DGX figure)
 
 # BASELINE config 5 (0.8B-shaped): hidden 1024, intermediate 3584, 24 layers.
 HIDDEN, INTER, LAYERS = 1024, 3584, 24
@@ -353,6 +354,18 @@ def single_kernel(name, tokens, device, seed=1):
         return (lambda: q.native_delta_gates(proj, Z_OFF + HV * DV, HV, a_decay, dt_bias, beta=beta,
                                              decay=decay, ctx=ctx),
                 4 * T * HV * 4)
+    if name in ("bf16_to_f32", "f32_to_bf16"):
+        # `tokens` rows of HIDDEN: the embedding table (VOCAB rows) for the
+        # weight upload widen, activations for the encode
+        n = T * HIDDEN
+        if name == "bf16_to_f32":
+            bits = torch.randint(-32768, 32768, (n,), generator=g, device=device, dtype=torch.int32)
+            bits = bits.to(torch.int16)
+            out = torch.empty(n, **f)
+            return lambda: q.native_bf16_to_f32(bits, out=out, ctx=ctx), 6 * n
+        x = normal((n,))
+        out = torch.empty(n, dtype=torch.bfloat16, device=device)
+        return lambda: q.native_f32_to_bf16(x, out=out, ctx=ctx), 6 * n
     raise SystemExit(f"unknown kernel {name}")
 
 
@@ -368,11 +381,11 @@ def kernel_sets(name, tokens, device, max_sets=8):
     return [fn] + [single_kernel(name, tokens, device, seed=1 + i)[0] for i in range(1, sets)], nbytes
 
 
-def time_launches(fns, device, reps, warmup=3):
-    """Average device time (us) of `reps` back-to-back launches cycling over
-    the input sets `fns`, replayed as one captured CUDA graph so that the
-    host's per-call cost (argument checks, ctypes) cannot leave the GPU idle
-    between short launches."""
+def time_launches(fns, device, reps, warmup=3, repeats=21):
+    """Median over `repeats` of the average device time (us) of `reps`
+    back-to-back launches cycling over the input sets `fns`, replayed as one
+    captured CUDA graph so that the host's per-call cost (argument checks,
+    ctypes) cannot leave the GPU idle between short launches."""
     import torch
     for i in range(warmup):
         fns[i % len(fns)]()
@@ -382,15 +395,18 @@ def time_launches(fns, device, reps, warmup=3):
     with torch.cuda.graph(graph, stream=stream):
         for i in range(reps):
             fns[i % len(fns)]()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(repeats)]
     with torch.cuda.stream(stream):
         graph.replay()  # warm: first replay uploads the graph
-        s.record()
-        graph.replay()
-        e.record()
+        for s, e in events:
+            s.record()
+            graph.replay()
+            e.record()
     torch.cuda.synchronize(device)
     del graph
-    return s.elapsed_time(e) * 1e3 / reps
+    times = sorted(s.elapsed_time(e) * 1e3 / reps for s, e in events)
+    return times[len(times) // 2]
 
 
 CONFIG_CASES = [  # (report name, kernel, tokens)
@@ -405,10 +421,14 @@ CONFIG_CASES = [  # (report name, kernel, tokens)
     # output gate at config-5 shapes
     ("cfg5_delta_conv_norm", "delta_conv_norm", 32768),
     ("cfg5_attn_gate", "attn_gate", 16384),
+    # weight upload: the config-5 embedding table (151936 x 1024) widened
+    # from its BF16 bits on the device; bf16 storage of activations
+    ("upload_embedding_bf16_to_f32", "bf16_to_f32", VOCAB),
+    ("cfg4_activations_f32_to_bf16", "f32_to_bf16", 32768),
 ]
 
 
-def kernel_configs(device, peak, reps=20):
+def kernel_configs(device, peak, reps=50):
     """BASELINE configs 2-4 as single-kernel workloads: GB/s and fraction of
     the HBM peak, each averaged over `reps` back-to-back launches that cycle
     over independent input sets, >= 3 x L2 touched before a set is reused."""
@@ -419,7 +439,8 @@ def kernel_configs(device, peak, reps=20):
         us = time_launches(fns, device, reps)
         gbs = nbytes / (us * 1e-6) / 1e9
         out[label] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
-                      "bytes": nbytes, "input_sets": len(fns)}
+                      "frac_of_spec": round(gbs / SPEC_HBM_GBS, 4), "bytes": nbytes,
+                      "input_sets": len(fns)}
         del fns
         torch.cuda.empty_cache()
     return out
@@ -437,7 +458,8 @@ def run_single_kernel(args):
     print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "launches": args.warmup + 2 * args.steps,
                       "input_sets": len(fns),
                       "us_per_launch": round(us, 2), "bytes_per_launch": nbytes,
-                      "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "peak": peak,
+                      "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
+                      "frac_of_spec": round(gbs / SPEC_HBM_GBS, 4), "peak": peak,
                       "peak_kind": kind}), flush=True)
 
 
@@ -599,7 +621,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel alone (gather_rms[_bf16], post_rms[_bf16], swiglu, "
                          "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope, "
-                         "delta_conv_norm, attn_gate, delta_gates)")
+                         "delta_conv_norm, attn_gate, delta_gates, bf16_to_f32, f32_to_bf16)")
     ap.add_argument("--tokens", type=int, default=16384, help="rows for --kernel")
     ap.add_argument("--no-forward", action="store_true", help="skip the whole-forward tokens/s leg")
     ap.add_argument("--forward-steps", type=int, default=2)
@@ -816,9 +838,11 @@ def main():
                       "(L2 126 MB); timed as back-to-back CUDA-graph replays",
             },
             "frac_of_hbm": round(value / (world * peak), 4),
+            "frac_of_spec": round(value / (world * SPEC_HBM_GBS), 4),
             "roofline": {"bound": "hbm", "kernel": "swiglu (silu(gate)*up, 32768x3584-class rows)",
                          "achieved": round(dom_achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(dom_achieved / peak, 4),
+                         "frac_of_spec": round(dom_achieved / SPEC_HBM_GBS, 4),
                          "traffic": round(T * SWIGLU_DRAM_BYTES_PER_TOKEN),
                          "traffic_note": "dram read+write of one ncu capture at 16384 tokens "
                                          "(bench.py --kernel swiglu --tokens 16384) scaled to this launch's "

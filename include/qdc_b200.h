@@ -269,6 +269,18 @@ QDC_API int qdc_delta_conv_norm(qdc_ctx *ctx, float *q_out, float *k_out,
                                 int key_dim, int value_heads, int value_dim,
                                 float eps, void *stream);
 
+/* bf16 storage <-> Float32 on the device, n elements, out and in not
+ * overlapping.  qdc_bf16_to_f32: out = bits << 16 (src/safetensors.jl:28-30),
+ * exact -- the weight upload path: a checkpoint's raw BF16 bytes are copied
+ * to the device and widened there, half the host -> device traffic of the
+ * reference's host-side decode (src/safetensors.jl:3-35).  qdc_f32_to_bf16:
+ * round to nearest even by integer add, no NaN special case
+ * (src/safetensors.jl:38-42), for bf16-stored activations. */
+QDC_API int qdc_bf16_to_f32(qdc_ctx *ctx, float *out, const uint16_t *in, int64_t n,
+                            void *stream);
+QDC_API int qdc_f32_to_bf16(qdc_ctx *ctx, uint16_t *out, const float *in, int64_t n,
+                            void *stream);
+
 /* SwiGLU gate:  h = silu(g) * u  (src/backbone.jl:196-197,352-355).
  * g/u rows at g + t*ld_g, u + t*ld_u (the packed [gate;up] projection of
  * ext/cuda_mlp.jl:63-71 is g = P, u = P + width, ld = 2*width).  Writes

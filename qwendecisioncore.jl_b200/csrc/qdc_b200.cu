@@ -113,6 +113,8 @@ int resident_blocks(const void* kernel, int device, int threads) {
 // warps (at 8192 rows a full wave of 3552 warps would leave the third round
 // 31% busy).
 int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units) {
+    if (units < 1) units = 1;
+    if (work_per_block_units < 1) work_per_block_units = 1;
     const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, qdc::kThreads);
     const int64_t per_wave = cap * work_per_block_units;
     const int64_t rounds = (units + per_wave - 1) / per_wave;
@@ -764,6 +766,40 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
     auto k = qdc::delta_conv_norm_generic;
     const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
     return launch(ctx, k, grid, a, stream, "delta_conv_norm");
+}
+
+// ------------------------------------------------------- bf16 <-> Float32
+
+namespace {
+int convert(qdc_ctx* ctx, void* out, const void* in, int64_t n, bool widen, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (n < 0) return fail(ctx, QDC_EINVAL, "negative element count %lld", (long long)n);
+    if (n == 0) return QDC_OK;
+    if (!out || !in) return fail(ctx, QDC_EINVAL, "out and in are required");
+    const uintptr_t o = reinterpret_cast<uintptr_t>(out), i = reinterpret_cast<uintptr_t>(in);
+    const size_t out_bytes = size_t(n) * (widen ? 4 : 2), in_bytes = size_t(n) * (widen ? 2 : 4);
+    if (o < i + in_bytes && i < o + out_bytes) return fail(ctx, QDC_EINVAL, "out and in overlap");
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    const bool vec = aligned16(out) && aligned16(in);
+    void (*k)(qdc::ConvertArgs) = widen ? (vec ? qdc::bf16_widen<true> : qdc::bf16_widen<false>)
+                                        : (vec ? qdc::bf16_encode<true> : qdc::bf16_encode<false>);
+    // units of work per thread step: kConvertUnroll groups of 8 elements
+    // (vector) or single elements
+    int64_t items = vec ? (n / 8 + qdc::kConvertUnroll - 1) / qdc::kConvertUnroll : n;
+    if (items < 1) items = 1;  // n < 8: the tail loop alone
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads, items);
+    qdc::ConvertArgs a{out, in, n};
+    return launch(ctx, k, grid, a, stream, widen ? "bf16_to_f32" : "f32_to_bf16");
+}
+}  // namespace
+
+int qdc_bf16_to_f32(qdc_ctx* ctx, float* out, const uint16_t* in, int64_t n, void* stream) {
+    return convert(ctx, out, in, n, true, stream);
+}
+
+int qdc_f32_to_bf16(qdc_ctx* ctx, uint16_t* out, const float* in, int64_t n, void* stream) {
+    return convert(ctx, out, in, n, false, stream);
 }
 
 // ------------------------------------------------------------------ SwiGLU

@@ -982,6 +982,82 @@ static __global__ void __launch_bounds__(kThreads) delta_gates(DeltaGateArgs a) 
     }
 }
 
+// ------------------------------------------------------ bf16 <-> Float32
+// Weight upload and bf16 activation storage: widen bf16 bits to Float32 as
+// bits << 16 (src/safetensors.jl:28-30) or encode Float32 to bf16 by the
+// round-to-nearest-even integer add (:38-42).  VEC kernels: groups of 8
+// elements (16 bytes of bf16, 32 bytes of Float32), both pointers 16-byte
+// aligned, kConvertUnroll groups per thread per step with every load issued
+// before any store; elements past the last whole group are done one per
+// thread.  Persistent grid-stride.
+
+constexpr int kConvertUnroll = 4;
+
+struct ConvertArgs {
+    void* out;
+    const void* in;
+    int64_t n;
+};
+
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads) bf16_widen(ConvertArgs a) {
+    pdl_enter();
+    constexpr int U = kConvertUnroll;
+    const int64_t threads = int64_t(gridDim.x) * blockDim.x;
+    const int64_t tid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint16_t* in = static_cast<const uint16_t*>(a.in);
+    float* out = static_cast<float*>(a.out);
+    const int64_t groups = VEC ? a.n / 8 : 0;
+    for (int64_t g0 = tid; g0 < groups; g0 += threads * U) {
+        uint4 r[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int64_t g = g0 + k * threads;
+            if (g < groups) r[k] = ld_nc_u4(in + 8 * g);
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int64_t g = g0 + k * threads;
+            if (g < groups) {
+                st_f4(out + 8 * g, make_float4(bf16_lo(r[k].x), bf16_hi(r[k].x), bf16_lo(r[k].y), bf16_hi(r[k].y)));
+                st_f4(out + 8 * g + 4,
+                      make_float4(bf16_lo(r[k].z), bf16_hi(r[k].z), bf16_lo(r[k].w), bf16_hi(r[k].w)));
+            }
+        }
+    }
+    for (int64_t i = 8 * groups + tid; i < a.n; i += threads) out[i] = __uint_as_float(uint32_t(in[i]) << 16);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads) bf16_encode(ConvertArgs a) {
+    pdl_enter();
+    constexpr int U = kConvertUnroll;
+    const int64_t threads = int64_t(gridDim.x) * blockDim.x;
+    const int64_t tid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const float* in = static_cast<const float*>(a.in);
+    uint16_t* out = static_cast<uint16_t*>(a.out);
+    const int64_t groups = VEC ? a.n / 8 : 0;
+    for (int64_t g0 = tid; g0 < groups; g0 += threads * U) {
+        float4 lo[U], hi[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int64_t g = g0 + k * threads;
+            if (g < groups) {
+                lo[k] = ld_nc_f4(in + 8 * g);
+                hi[k] = ld_nc_f4(in + 8 * g + 4);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int64_t g = g0 + k * threads;
+            if (g < groups)
+                st_u4(out + 8 * g, make_uint4(bf16_pack(lo[k].x, lo[k].y), bf16_pack(lo[k].z, lo[k].w),
+                                              bf16_pack(hi[k].x, hi[k].y), bf16_pack(hi[k].z, hi[k].w)));
+        }
+    }
+    for (int64_t i = 8 * groups + tid; i < a.n; i += threads) out[i] = uint16_t(bf16_bits(in[i]));
+}
+
 // ---------------------------------------------------------------- SwiGLU
 
 struct SwigluArgs {

@@ -74,6 +74,8 @@ SIGNATURES = {
     "qdc_gated_rms": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _vp],
     "qdc_attn_gate": [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _i64, _i64, _i64, _i64, _i64, _i64,
                       _vp],
+    "qdc_bf16_to_f32": [_vp, _vp, _vp, _i64, _vp],
+    "qdc_f32_to_bf16": [_vp, _vp, _vp, _i64, _vp],
     "qdc_delta_gates": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _vp],
     "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
                             _flt, _vp],

@@ -36,15 +36,14 @@ import torch.nn.functional as F
 
 from . import ops
 from ._lib import ArgumentError
-from .model import Config, load_weights, pack_layers, random_weights
+from .model import Config, device_f32, load_weights, pack_layers, random_weights
 
 FLOATMAX32 = float(np.finfo(np.float32).max)
 DELTA_CHUNK = 64  # src/backbone.jl:301, ext/cuda_delta_chunked.jl:9
 
 
 def _device_f32(x, device):
-    t = x if torch.is_tensor(x) else torch.from_numpy(np.ascontiguousarray(x, np.float32))
-    return t.to(device=device, dtype=torch.float32).contiguous()
+    return device_f32(x, device)
 
 
 def check_sequence(vocab, ids, mask):
@@ -78,7 +77,9 @@ class QwenBackbone:
 
     @classmethod
     def from_directory(cls, directory, device="cuda"):
-        config, weights = load_weights(directory)
+        """QwenBackbone(dir; device) (src/backbone.jl:74-192).  BF16 checkpoint
+        tensors are uploaded as their raw bits and widened on the device."""
+        config, weights = load_weights(directory, raw_bf16=torch.device(device).type == "cuda")
         return cls(config, weights, device)
 
     @classmethod

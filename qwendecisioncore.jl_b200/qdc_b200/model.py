@@ -87,9 +87,11 @@ class Config:
         return 2 * self.key_width + self.value_width
 
 
-def read_safetensors(path, select=None):
+def read_safetensors(path, select=None, raw_bf16=False):
     """name -> float32 numpy array, row-major as stored (src/safetensors.jl:3-35).
-    F32 / F16 widen exactly; BF16 widens as bits << 16 (:28-30)."""
+    F32 / F16 widen exactly; BF16 widens as bits << 16 (:28-30), or with
+    `raw_bf16` stays as its uint16 bits, to be copied to a device as they are
+    and widened there (`device_f32`)."""
     out = {}
     size = os.path.getsize(path)
     with open(path, "rb") as f:
@@ -113,7 +115,9 @@ def read_safetensors(path, select=None):
                 raise ValueError(f"Invalid size for tensor {name}.")
             f.seek(base + start)
             raw = np.frombuffer(f.read(stop - start), dtype)
-            if spec["dtype"] == "BF16":
+            if spec["dtype"] == "BF16" and raw_bf16:
+                arr = raw.copy()
+            elif spec["dtype"] == "BF16":
                 arr = (raw.astype(np.uint32) << 16).view(np.float32)
             else:
                 arr = raw.astype(np.float32)
@@ -121,11 +125,12 @@ def read_safetensors(path, select=None):
     return out
 
 
-def load_weights(directory):
+def load_weights(directory, raw_bf16=False):
     """(Config, {canonical name: float32 array}) from a checkpoint directory:
     config.json + model.safetensors or the shards of
     model.safetensors.index.json, `language_model.` prefix canonicalised
-    (src/backbone.jl:107-135)."""
+    (src/backbone.jl:107-135).  `raw_bf16`: BF16 tensors stay uint16 bits
+    (read_safetensors)."""
     with open(os.path.join(directory, "config.json")) as f:
         config = Config.from_json(json.load(f))
     single = os.path.join(directory, "model.safetensors")
@@ -140,7 +145,7 @@ def load_weights(directory):
         files = [os.path.join(directory, s) for s in shards]
     weights = {}
     for path in files:
-        for name, value in read_safetensors(path, lambda n: "language_model." in n).items():
+        for name, value in read_safetensors(path, lambda n: "language_model." in n, raw_bf16).items():
             weights[name[name.find("language_model.") + len("language_model."):]] = value
     return config, weights
 
@@ -189,9 +194,17 @@ def random_weights(cfg, seed=0, std=0.02, device="cpu"):
     return w
 
 
-def _t(x, device):
+def device_f32(x, device):
+    """A Float32 tensor on `device` from a tensor or a numpy array.  uint16
+    arrays are BF16 bits (read_safetensors(raw_bf16=True)): they are copied
+    to the GPU as they are and widened there by qdc_bf16_to_f32, half the
+    host -> device bytes of widening on the host."""
     if torch.is_tensor(x):
         return x.to(device=device, dtype=torch.float32).contiguous()
+    if x.dtype == np.uint16:
+        from . import ops
+        bits = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(device)
+        return ops.native_bf16_to_f32(bits)
     return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(device)
 
 
@@ -199,7 +212,7 @@ def pack_layers(cfg, weights, device):
     """Device weights per layer, projections packed so each block is one
     GEMM (the packing of ext/cuda_mlp.jl:9-47)."""
     layers = []
-    take = lambda name: _t(weights[name], device)
+    take = lambda name: device_f32(weights[name], device)
     for i, kind in enumerate(cfg.layer_types):
         p = f"layers.{i}."
         layer = {

@@ -468,6 +468,46 @@ def native_attn_gate(values, gate, *, out=None, ctx=None, stream=None):
     return out
 
 
+_BF16_BITS = (torch.bfloat16, torch.int16, torch.uint16)
+
+
+def native_bf16_to_f32(bits, *, out=None, ctx=None, stream=None):
+    """Float32 = bf16 bits << 16 (src/safetensors.jl:28-30), on the device:
+    `bits` is a contiguous CUDA tensor of bfloat16 or of raw 16-bit words
+    (int16 / uint16), e.g. a checkpoint's BF16 bytes copied as they are.
+    Returns a Float32 tensor of the same shape."""
+    dev = _cuda(bits, out)
+    if bits.dtype not in _BF16_BITS or not bits.is_contiguous():
+        raise ArgumentError(_lib.QDC_EINVAL, "bits must be a contiguous bfloat16 / int16 / uint16 tensor")
+    if out is None:
+        out = torch.empty(bits.shape, dtype=torch.float32, device=dev)
+    elif out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != bits.numel():
+        raise DimensionMismatch(_lib.QDC_EINVAL, "out must be a contiguous Float32 tensor of as many elements")
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_bf16_to_f32(ctx.handle, _ptr(out), _ptr(bits), bits.numel(), _stream(dev, stream)),
+              ctx.handle)
+    return out
+
+
+def native_f32_to_bf16(x, *, out=None, ctx=None, stream=None):
+    """bf16 storage of Float32 `x` by the reference's round-to-nearest-even
+    integer add, no NaN special case (src/safetensors.jl:38-42).  Returns a
+    bfloat16 tensor of the same shape (`out` may be bfloat16 / int16 / uint16)."""
+    dev = _cuda(x, out)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ArgumentError(_lib.QDC_EINVAL, "x must be a contiguous Float32 tensor")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=dev)
+    elif out.dtype not in _BF16_BITS or not out.is_contiguous() or out.numel() != x.numel():
+        raise DimensionMismatch(_lib.QDC_EINVAL, "out must be a contiguous 16-bit tensor of as many elements")
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_f32_to_bf16(ctx.handle, _ptr(out), _ptr(x), x.numel(), _stream(dev, stream)),
+              ctx.handle)
+    return out
+
+
 def native_delta_gates(proj, start, heads, a_decay, dt_bias, *, beta=None, decay=None, ctx=None,
                        stream=None):
     """beta = sigmoid(b), decay = a_decay * softplus(a + dt_bias) per (token,

@@ -200,7 +200,8 @@ def test_config_validation():
 
 
 def test_safetensors_bf16_decode(tmp_path, oracle):
-    """BF16 tensors widen as bits << 16 (src/safetensors.jl:28-30)."""
+    """BF16 tensors widen as bits << 16 (src/safetensors.jl:28-30), or stay
+    their raw bits for a device-side widen."""
     import json
     import struct
     from qdc_b200.model import read_safetensors
@@ -211,3 +212,6 @@ def test_safetensors_bf16_decode(tmp_path, oracle):
     path.write_bytes(struct.pack("<Q", len(header)) + header + bits.tobytes())
     got = read_safetensors(str(path))["w"]
     assert np.array_equal(got.reshape(-1), oracle.bf16_decode(bits))
+    raw = read_safetensors(str(path), raw_bf16=True)["w"]
+    assert raw.dtype == np.uint16 and raw.shape == (2, 2)
+    assert np.array_equal(raw.reshape(-1), bits)

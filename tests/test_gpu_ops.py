@@ -7,9 +7,13 @@ layouts, NaN-filled outputs that must be overwritten, inputs unchanged) plus
 the BASELINE shapes (hidden 1024, head_dim 256 / rotary 64, Dv 128,
 intermediate 3584).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
+
+from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
 
@@ -514,3 +518,85 @@ def test_misaligned_gamma_takes_scalar_kernels(q, oracle):
     gq, gk = q.native_q_k_norm_rope(dev(qi), dev(ki), _misaligned(wq), dev(wk), 1e-6, 64, dc, ds)
     assert f32_close(gq, oracle.qk_norm_rope(qi, wq, 1e-6, 64, cos, sin))
     assert f32_close(gk, oracle.qk_norm_rope(ki, wk, 1e-6, 64, cos, sin))
+
+
+# ----------------------------------------------------------- bf16 storage
+
+@pytest.mark.parametrize("offset", [0, 1, 3])
+def test_bf16_widen_every_pattern(q, offset):
+    """qdc_bf16_to_f32 = bits << 16 (src/safetensors.jl:28-30) for all 65,536
+    patterns (NaN payloads included), aligned and misaligned, odd lengths."""
+    bits = np.arange(65536 + 5, dtype=np.uint32).astype(np.uint16)
+    buf = torch.from_numpy(np.concatenate([np.zeros(offset, np.uint16), bits]).view(np.int16)).cuda()
+    src = buf[offset:]
+    got = q.native_bf16_to_f32(src)
+    expected = (bits.astype(np.uint32) << 16)
+    assert np.array_equal(got.cpu().numpy().view(np.uint32), expected)
+    out = torch.zeros(7, device="cuda")
+    q.native_bf16_to_f32(src[:7], out=out)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), expected[:7])
+    assert q.native_bf16_to_f32(src[:0]).numel() == 0
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+def test_bf16_encode_matches_reference_rounding(q, oracle, offset):
+    """qdc_f32_to_bf16: round to nearest even by integer add, no NaN special
+    case (src/safetensors.jl:38-42), bit-exact with the oracle."""
+    r = rng(9)
+    x = np.concatenate([r.normal(0, 1, 40001).astype(np.float32),
+                        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8,
+                                  3.4028235e38, 1e-40, -1e-40], np.float32),
+                        (np.arange(4096, dtype=np.uint32) * 0x00010001 + 0x7fff).view(np.float32)])
+    buf = torch.from_numpy(np.concatenate([np.zeros(offset, np.float32), x])).cuda()
+    got = q.native_f32_to_bf16(buf[offset:])
+    assert got.dtype == torch.bfloat16
+    assert np.array_equal(got.view(torch.int16).cpu().numpy().view(np.uint16), oracle.bf16_encode(x))
+
+
+def test_bf16_converters_reject_overlap_and_bad_types(q):
+    t = torch.zeros(64, device="cuda")
+    with pytest.raises(q.ArgumentError):
+        q.native_bf16_to_f32(t)                      # Float32 is not bf16 bits
+    with pytest.raises(q.ArgumentError):
+        q.native_f32_to_bf16(t.view(torch.int32))    # not Float32
+    with pytest.raises(q.ArgumentError):             # out overlaps in
+        q.native_f32_to_bf16(t, out=t.view(torch.bfloat16)[:64])
+
+
+def _write_bf16_checkpoint(src_dir, dst_dir, oracle):
+    """The fixture checkpoint with every tensor stored as BF16."""
+    import json
+    import shutil
+    import struct
+    from qdc_b200.model import read_safetensors
+    shutil.copyfile(os.path.join(src_dir, "config.json"), os.path.join(dst_dir, "config.json"))
+    tensors = read_safetensors(os.path.join(src_dir, "model.safetensors"))
+    header, blobs, off = {}, [], 0
+    for name, arr in tensors.items():
+        bits = oracle.bf16_encode(np.ascontiguousarray(arr, np.float32).reshape(-1)).tobytes()
+        header[name] = {"dtype": "BF16", "shape": list(arr.shape), "data_offsets": [off, off + len(bits)]}
+        blobs.append(bits)
+        off += len(bits)
+    h = json.dumps(header).encode()
+    with open(os.path.join(dst_dir, "model.safetensors"), "wb") as f:
+        f.write(struct.pack("<Q", len(h)) + h + b"".join(blobs))
+
+
+def test_bf16_checkpoint_upload_matches_host_widening(q, oracle, tmp_path):
+    """from_directory uploads BF16 tensors as raw bits and widens them on the
+    device; the model equals one built from host-widened weights."""
+    from qdc_b200.model import load_weights
+    _write_bf16_checkpoint(GOLDEN, str(tmp_path), oracle)
+    dev_model = q.QwenBackbone.from_directory(str(tmp_path), device="cuda")
+    cfg, host_w = load_weights(str(tmp_path))           # widened on the host
+    _, raw_w = load_weights(str(tmp_path), raw_bf16=True)
+    assert raw_w["embed_tokens.weight"].dtype == np.uint16
+    host_model = q.QwenBackbone(cfg, host_w, device="cuda")
+    assert torch.equal(dev_model.embedding, host_model.embedding)
+    for a, b in zip(dev_model.layers, host_model.layers):
+        for k in a:
+            if torch.is_tensor(a[k]):
+                assert torch.equal(a[k], b[k]), k
+    ids = (np.arange(33) * 5) % 64
+    mask = np.ones(33, np.int64)
+    assert np.array_equal(q.backbone_hidden(dev_model, ids, mask), q.backbone_hidden(host_model, ids, mask))

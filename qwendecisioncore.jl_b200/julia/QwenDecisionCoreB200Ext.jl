@@ -237,6 +237,19 @@ function delta_conv_norm!(query::CUDA.CuArray{Float32,3}, key::CUDA.CuArray{Floa
     return query, key, value
 end
 
+"""upload_bf16(bits::Array{UInt16}) -> CuArray{Float32}: a checkpoint's raw
+BF16 words copied to the device as they are and widened there (bits << 16,
+src/safetensors.jl:28-30), half the host -> device bytes of widening on the
+host before native_array(::Val{:cuda}, x) (ext/QwenDecisionCoreCUDAExt.jl:7)."""
+function upload_bf16(bits::Array{UInt16})
+    dev_bits = CUDA.CuArray(bits)
+    out = CUDA.CuArray{Float32}(undef, size(bits))
+    ctx = context()
+    check(ccall((:qdc_bf16_to_f32, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Ptr{Cvoid}),
+                ctx.handle, ptr(out), ptr(dev_bits), Int64(length(bits)), stream_handle()), ctx.handle)
+    return out
+end
+
 """sync!() -- the synchronize of native_forward_scope's `finally`
 (ext/cuda_workspace.jl:62-66), reporting device-side id errors."""
 sync!() = check(ccall((:qdc_sync, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}), context().handle,
@@ -251,7 +264,7 @@ function __init__()
         cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!,
                                                           qk_norm_rope!, rope_tables, gated_rms!,
                                                           swiglu!, attn_gate!, delta_gates!,
-                                                          delta_conv_norm!, sync!))
+                                                          delta_conv_norm!, upload_bf16, sync!))
     end
 end
 

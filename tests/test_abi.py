@@ -51,6 +51,10 @@ def test_null_context_is_rejected_without_touching_the_device(lib):
                                 None) == 1
     assert lib.qdc_swiglu(None, None, None, None, None, 1, 4, 4, 4, 4, None) == 1
     assert lib.qdc_ws_alloc(None, 16, 256, ctypes.byref(ctypes.c_void_p())) == 1
+    assert lib.qdc_set_option(None, 1, 0) == 1
+    assert lib.qdc_bf16_to_f32(None, None, None, 8, None) == 1
+    assert lib.qdc_f32_to_bf16(None, None, None, 8, None) == 1
+    assert lib.qdc_delta_gates(None, None, None, None, 16, 0, None, None, 1, 4, None) == 1
     assert b"NULL" in lib.qdc_last_error(None)
 
 

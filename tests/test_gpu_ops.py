@@ -600,3 +600,24 @@ def test_bf16_checkpoint_upload_matches_host_widening(q, oracle, tmp_path):
     ids = (np.arange(33) * 5) % 64
     mask = np.ones(33, np.int64)
     assert np.array_equal(q.backbone_hidden(dev_model, ids, mask), q.backbone_hidden(host_model, ids, mask))
+
+
+def test_pdl_option(q, oracle):
+    """QDC_OPT_PDL off launches the same kernels without programmatic
+    dependent launch: identical results; an unknown option is refused."""
+    from qdc_b200 import _lib
+    ctx = q.context(torch.device("cuda", 0))
+    assert ctx.pdl
+    r = rng(3)
+    x = r.normal(0, 1, (300, 1024)).astype(np.float32)
+    m = r.normal(0, 1, (300, 1024)).astype(np.float32)
+    w = r.normal(0, 0.02, 1024).astype(np.float32)
+    on = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
+    try:
+        ctx.pdl = False
+        off = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
+    finally:
+        ctx.pdl = True
+    assert torch.equal(on[0], off[0]) and torch.equal(on[1], off[1])
+    with pytest.raises(q.ArgumentError):
+        _lib.check(ctx.lib.qdc_set_option(ctx.handle, 99, 1), ctx.handle)

@@ -75,10 +75,11 @@ QDC_API int qdc_destroy(qdc_ctx *ctx);
 
 /* Context options (value 0 = off, nonzero = on); QDC_EINVAL for an unknown
  * option.
- * QDC_OPT_PDL (default on): launch this context's kernels with programmatic
- * dependent launch, so each overlaps its launch and ramp with the preceding
- * kernel's drain; every kernel still waits for its predecessor grid to
- * complete before it touches global memory. */
+ * QDC_OPT_PDL (default off): launch this context's kernels with programmatic
+ * dependent launch, so a kernel's CTAs may become resident while the
+ * preceding kernel drains; every kernel still waits for its predecessor grid
+ * to complete before it touches global memory.  Off by default because the
+ * persistent grids fill the SMs and measured no gain. */
 #define QDC_OPT_PDL 1
 QDC_API int qdc_set_option(qdc_ctx *ctx, int option, int value);
 

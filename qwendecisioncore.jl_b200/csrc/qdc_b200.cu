@@ -21,7 +21,7 @@
 struct qdc_ctx {
     int device = -1;
     int sm_count = 0;
-    bool pdl = true;  // QDC_OPT_PDL
+    bool pdl = false;  // QDC_OPT_PDL
     std::string err;
     // workspace arena
     char* arena = nullptr;
@@ -124,8 +124,8 @@ int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int
     return int(g < 1 ? 1 : g);
 }
 
-// Launch, with programmatic stream serialization unless the context turned
-// it off (QDC_OPT_PDL; see qdc_kernels.cuh).
+// Launch, with programmatic stream serialization when the context turned it
+// on (QDC_OPT_PDL; see qdc_kernels.cuh).
 template <typename Args>
 int launch(qdc_ctx* ctx, void (*kernel)(Args), int grid, const Args& args, void* stream,
            const char* name, int threads = qdc::kThreads, size_t smem = 0) {

@@ -30,13 +30,15 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kThreads = 256;  // 8 warps per CTA for the vector kernels
 
 // ------------------------------------------------ programmatic dependent launch
-// A context launches its kernels with programmatic stream serialization
-// (QDC_OPT_PDL, on by default): a kernel's CTAs may become resident while
-// its predecessor kernel drains.  Each kernel first waits for the predecessor grid to
-// complete (griddepcontrol.wait -- a no-op when launched without the
-// attribute) and only then touches global memory, then lets its own
-// successor start launching.  This hides the launch and ramp of each of the
-// ~100 kernels of a forward step.
+// With QDC_OPT_PDL a context launches its kernels with programmatic stream
+// serialization: a kernel's CTAs may become resident while its predecessor
+// drains.  Each kernel first waits for the predecessor grid to complete
+// (griddepcontrol.wait -- a no-op when launched without the attribute) and
+// only then touches global memory, then lets its own successor start
+// launching.  The option is off by default: these persistent grids fill
+// every SM, so a successor's CTAs find no room until the predecessor's exit,
+// and chains of row kernels measured a 2.9 us fixed cost per launch with it
+// against 2.4 us without.
 __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -52,11 +52,11 @@ class Context:
         check(self.lib.qdc_init(self.device.index or 0, ctypes.byref(handle)))
         self.handle = handle
         self.lock = threading.RLock()
-        self._pdl = True
+        self._pdl = False
 
     @property
     def pdl(self):
-        """Programmatic dependent launch of this context's kernels (on by
+        """Programmatic dependent launch of this context's kernels (off by
         default; QDC_OPT_PDL of include/qdc_b200.h)."""
         return self._pdl
 

@@ -457,9 +457,9 @@ def test_delta_gates_rejects_bad_columns(q):
 
 @pytest.mark.parametrize("width_heads", [16, 8])
 def test_row_kernel_waits_for_its_producer(q, oracle, width_heads):
-    """Kernels launch with programmatic dependent launch: a residual norm
-    issued right behind the gated norm that writes its input (a NaN-filled
-    buffer) must read the finished rows, never the fill."""
+    """With programmatic dependent launch on, a residual norm issued right
+    behind the gated norm that writes its input (a NaN-filled buffer) must
+    read the finished rows, never the fill."""
     T, H, D = 16384, width_heads, 128
     r = rng(T + H)
     o = r.normal(0, 1, (T, H, D)).astype(np.float32)
@@ -470,13 +470,18 @@ def test_row_kernel_waits_for_its_producer(q, oracle, width_heads):
     gated = oracle.gated_rms(o, z, wg, 1e-6)
     ex_r, ex_y = oracle.residual_rms(gated, m, wr, 1e-6)
     do, dz, dwg, dm, dwr = dev(o), dev(z), dev(wg), dev(m), dev(wr)
-    for _ in range(3):
-        g = nan_like((T, H * D))
-        q.native_gated_rms(do, dz, dwg, 1e-6, out=g)
-        rr, yy = q.native_residual_rms(g, dm, dwr, 1e-6, out_r=nan_like((T, H * D)),
-                                       out_y=nan_like((T, H * D)))
-        assert not torch.isnan(yy).any()
-        assert f32_close(rr, ex_r) and f32_close(yy, ex_y)
+    ctx = q.context(torch.device("cuda", 0))
+    try:
+        ctx.pdl = True  # QDC_OPT_PDL: the launch mode in which the wait matters
+        for _ in range(3):
+            g = nan_like((T, H * D))
+            q.native_gated_rms(do, dz, dwg, 1e-6, out=g, ctx=ctx)
+            rr, yy = q.native_residual_rms(g, dm, dwr, 1e-6, out_r=nan_like((T, H * D)),
+                                           out_y=nan_like((T, H * D)), ctx=ctx)
+            assert not torch.isnan(yy).any()
+            assert f32_close(rr, ex_r) and f32_close(yy, ex_y)
+    finally:
+        ctx.pdl = False
 
 
 def _misaligned(a):
@@ -603,21 +608,24 @@ def test_bf16_checkpoint_upload_matches_host_widening(q, oracle, tmp_path):
 
 
 def test_pdl_option(q, oracle):
-    """QDC_OPT_PDL off launches the same kernels without programmatic
-    dependent launch: identical results; an unknown option is refused."""
+    """QDC_OPT_PDL on launches the same kernels with programmatic dependent
+    launch: identical results; an unknown option is refused."""
     from qdc_b200 import _lib
     ctx = q.context(torch.device("cuda", 0))
-    assert ctx.pdl
+    assert not ctx.pdl
     r = rng(3)
     x = r.normal(0, 1, (300, 1024)).astype(np.float32)
     m = r.normal(0, 1, (300, 1024)).astype(np.float32)
     w = r.normal(0, 0.02, 1024).astype(np.float32)
-    on = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
+    off = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
     try:
-        ctx.pdl = False
-        off = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
-    finally:
         ctx.pdl = True
-    assert torch.equal(on[0], off[0]) and torch.equal(on[1], off[1])
+        g = nan_like((300, 1024))
+        q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, out_y=g, ctx=ctx)  # producer ...
+        on = q.native_residual_rms(g, dev(m), dev(w), 1e-6, ctx=ctx)       # ... and consumer
+        ref = q.native_residual_rms(off[1], dev(m), dev(w), 1e-6, ctx=ctx)
+    finally:
+        ctx.pdl = False
+    assert torch.equal(on[0], ref[0]) and torch.equal(on[1], ref[1])
     with pytest.raises(q.ArgumentError):
         _lib.check(ctx.lib.qdc_set_option(ctx.handle, 99, 1), ctx.handle)

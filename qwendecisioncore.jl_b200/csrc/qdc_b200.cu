@@ -22,6 +22,7 @@ struct qdc_ctx {
     int device = -1;
     int sm_count = 0;
     bool pdl = false;  // QDC_OPT_PDL
+    bool conv_smem_set = false;  // DeltaNet pipeline's dynamic shared memory limit raised
     std::string err;
     // workspace arena
     char* arena = nullptr;
@@ -738,10 +739,10 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
         tiles < (int64_t(1) << 32) - (int64_t(1) << 24)) {
         auto k = qdc::delta_conv_norm_pipe<PR, PS>;
         const int smem = PS * (PR + 3) * 512 * int(sizeof(float));
-        static bool attr_set[64] = {};
-        if (ctx->device < 64 && !attr_set[ctx->device]) {
+        // once per context (a context is used by one host thread at a time)
+        if (!ctx->conv_smem_set) {
             QDC_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            attr_set[ctx->device] = true;
+            ctx->conv_smem_set = true;
         }
         qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                         value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),

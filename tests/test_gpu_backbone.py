@@ -131,7 +131,7 @@ def cfg1_pair(q):
     return model, F.Model(ocfg, weights)
 
 
-@pytest.mark.parametrize("n", [1, 9, 63, 64, 65, 129])
+@pytest.mark.parametrize("n", [1, 9, 63, 64, 65, 129, 256, 257])
 @pytest.mark.parametrize("holes", [False, True])
 def test_config1_forward_matches_oracle(q, cfg1_pair, n, holes):
     from oracle import forward as F
@@ -245,3 +245,54 @@ def test_config1_every_kernel_site(q, cfg1_pair, oracle):
             ex_r, ex_y = oracle.residual_rms(cpu(ins[0]), cpu(ins[1]), gam, cfg.eps)
             assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), site
             layer += 1
+
+
+def test_last_hidden_shared_across_threads(q, fixture_model):
+    """Several host threads calling backbone_last_hidden on one model (the
+    reference shares its cached graphs across tasks, test/cuda.jl:33-46):
+    each result equals the one computed alone."""
+    import threading
+    cases = [((np.arange(n) * (3 + n)) % 64, np.ones(n, np.int64)) for n in (17, 17, 40, 40, 65, 9)]
+    alone = [q.backbone_last_hidden(fixture_model, i, m) for i, m in cases]
+    got = [None] * len(cases)
+    errors = []
+
+    def worker(k):
+        try:
+            for _ in range(3):
+                got[k] = q.backbone_last_hidden(fixture_model, *cases[k])
+        except Exception as e:  # surfaced below
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(k,)) for k in range(len(cases))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not errors and all(not t.is_alive() for t in threads)
+    for a, b in zip(got, alone):
+        assert np.array_equal(a, b)
+
+
+def test_delta_keys_64_wide(q):
+    """A synthetic hybrid backbone with 64-wide DeltaNet keys (test/cuda.jl:
+    67-93): the conv + norm takes its generic kernel; the forward matches the
+    oracle forward at the whole-forward bar."""
+    from oracle import forward as F
+    from qdc_b200.model import Config, random_weights
+    cfg = Config(hidden=128, head_dim=32, heads=4, kv_heads=2, key_heads=2, value_heads=4,
+                 key_dim=64, value_dim=32, eps=float(np.float32(1e-6)),
+                 rope_theta=float(np.float32(1e7)), rotary_dim=8, vocab=512, intermediate=256,
+                 layer_types=["linear_attention", "linear_attention", "full_attention"])
+    model = q.QwenBackbone.random(cfg, seed=3, device="cuda")
+    weights = {k: v.cpu().numpy() for k, v in random_weights(cfg, 3, device="cuda").items()}
+    ocfg = F.Config(**{k: getattr(cfg, k) for k in F.Config.__dataclass_fields__})
+    omodel = F.Model(ocfg, weights)
+    for n, holes in ((65, True), (130, False)):
+        ids = np.random.default_rng(n).integers(0, 512, n)
+        mask = np.ones(n, np.int64)
+        if holes:
+            mask[0:n - 1:3] = 0
+        expected = F.backbone_hidden(omodel, ids, mask)
+        assert _violation(q.backbone_hidden(model, ids, mask).astype(np.float64),
+                          expected.astype(np.float64)) <= 1.0

@@ -24,8 +24,9 @@ BF16_RTOL = 1e-2
 def f32_close(actual, expected):
     a = actual.detach().cpu().numpy().astype(np.float64) if torch.is_tensor(actual) else actual
     e = np.asarray(expected, np.float64)
-    ok = np.abs(a - e) <= ATOL + RTOL * np.abs(e)
-    ok |= np.isnan(a) & np.isnan(e)
+    with np.errstate(invalid="ignore"):
+        ok = np.abs(a - e) <= ATOL + RTOL * np.abs(e)
+    ok |= (np.isnan(a) & np.isnan(e)) | (a == e)  # NaN matches NaN; equal infinities match
     return bool(ok.all())
 
 
@@ -629,3 +630,25 @@ def test_pdl_option(q, oracle):
     assert torch.equal(on[0], ref[0]) and torch.equal(on[1], ref[1])
     with pytest.raises(q.ArgumentError):
         _lib.check(ctx.lib.qdc_set_option(ctx.handle, 99, 1), ctx.handle)
+
+
+@pytest.mark.parametrize("kd,vd", [(128, 128), (8, 6)])
+def test_delta_conv_norm_edge_values(q, oracle, kd, vd):
+    """The fused L2 norm on the reference's edge values (test/backbone.jl:
+    290-313): 0, -0, NaN, Inf, floatmax, the smallest subnormal, each token
+    its own sequence and a conv that passes the current token through, so
+    every head of token t holds silu(edge[t])."""
+    edges = np.array([0.0, -0.0, np.nan, np.inf, np.finfo(np.float32).max, 1e-45], np.float32)
+    kh, vh = 2, 4
+    C = 2 * kh * kd + vh * vd
+    proj = np.repeat(edges[:, None], C + 4, axis=1).astype(np.float32)
+    w = np.zeros((C, 4), np.float32)
+    w[:, 3] = 1.0  # taps oldest first: tap 3 is the current token
+    eq, ek, ev = oracle.delta_conv_norm(proj, w, kh, kd, vh, vd, seq_len=1)
+    gq, gk, gv = q.native_delta_conv_norm(dev(proj), dev(w), kh, kd, vh, vd, seq_len=1,
+                                          q_out=nan_like((6, kh, kd)), k_out=nan_like((6, kh, kd)),
+                                          v_out=nan_like((6, vh, vd)))
+    for got, exp in ((gq, eq), (gk, ek), (gv, ev)):
+        assert f32_close(got, exp)
+        a = got.cpu().numpy()
+        assert np.array_equal(np.isnan(a), np.isnan(exp)) and np.array_equal(np.isinf(a), np.isinf(exp))

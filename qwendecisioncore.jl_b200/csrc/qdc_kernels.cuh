@@ -743,9 +743,12 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         // thread tid copies 16-byte chunk (tid % 128) of rows tid / 128, +4, +8, ...
         const int col = (tid % (CH / 4)) * 4;
         constexpr int ROW_STEP = kConvPipeThreads / (CH / 4);
-        for (int row = tid / (CH / 4); row < ROWS; row += ROW_STEP) {
+        const int row1 = tid / (CH / 4);
+        const float* s_row = src + (t0 + row1) * a.ld + col;
+        const int64_t s_step = int64_t(ROW_STEP) * a.ld;
+        for (int row = row1; row < ROWS; row += ROW_STEP, s_row += s_step) {
             const int64_t t = t0 + row;
-            if (t >= 0 && t < a.tokens) cp_async16(dst + row * CH + col, src + t * a.ld + col);
+            if (t >= 0 && t < a.tokens) cp_async16(dst + row * CH + col, s_row);
         }
     };
 #pragma unroll
@@ -777,37 +780,13 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         for (int i = 0; i < TPW + 3; ++i) xr[i] = *reinterpret_cast<const float4*>(buf + i * CH);
         const int64_t t_first = int64_t(run) * R + r0;
         const int period = int(a.seq_div.d);
-        int pos = int(fmod(uint32_t(t_first), a.seq_div));
-        const int64_t dst_stride = h.group == 2 ? int64_t(a.vh) * a.vd : int64_t(a.kh) * a.kd;
+        const int pos0 = int(fmod(uint32_t(t_first), a.seq_div));
+        const int64_t left = a.tokens - t_first;
+        const int nr = left < TPW ? int(left) : TPW;  // tokens of this warp (<= 0: none)
+        const int dst_stride = h.group == 2 ? a.vh * a.vd : a.kh * a.kd;
         float* dst = conv_dst(a, h, t_first) + lane * 4;
-#pragma unroll
-        for (int r = 0; r < TPW; ++r) {
-            if (t_first + r >= a.tokens) break;
-            float4 acc;
-            if (pos >= 3) {  // all four taps inside the sequence: one FMA chain per channel
-                acc.x = __fmul_rn(xr[r].x, wt[0].x);
-                acc.y = __fmul_rn(xr[r].y, wt[1].x);
-                acc.z = __fmul_rn(xr[r].z, wt[2].x);
-                acc.w = __fmul_rn(xr[r].w, wt[3].x);
-#pragma unroll
-                for (int j = 1; j < 4; ++j) {
-                    acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
-                    acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
-                    acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
-                    acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
-                }
-            } else {  // the first tokens of a sequence: taps before its start are absent
-                acc = make_float4(0, 0, 0, 0);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (pos >= 3 - j) {
-                        acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
-                        acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
-                        acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
-                        acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
-                    }
-                }
-            }
+        // SiLU, the head's L2 norm for q / k, and the store of token r
+        auto finish = [&](int r, float4 acc) {
             acc.x = silu(acc.x);
             acc.y = silu(acc.y);
             acc.z = silu(acc.z);
@@ -826,7 +805,59 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
                 acc.w = __fmul_rn(acc.w, scale);
             }
             st_f4(dst + r * dst_stride, acc);
-            pos = pos + 1 == period ? 0 : pos + 1;
+        };
+        if (nr == TPW && pos0 >= 3 && pos0 + TPW <= period) {
+            // the common case: every token of the run has all four taps inside
+            // its sequence -- one FMA chain per channel, no per-token branch
+#pragma unroll
+            for (int r = 0; r < TPW; ++r) {
+                float4 acc;
+                acc.x = __fmul_rn(xr[r].x, wt[0].x);
+                acc.y = __fmul_rn(xr[r].y, wt[1].x);
+                acc.z = __fmul_rn(xr[r].z, wt[2].x);
+                acc.w = __fmul_rn(xr[r].w, wt[3].x);
+#pragma unroll
+                for (int j = 1; j < 4; ++j) {
+                    acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
+                    acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
+                    acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
+                    acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
+                }
+                finish(r, acc);
+            }
+        } else {
+            int pos = pos0;
+#pragma unroll
+            for (int r = 0; r < TPW; ++r) {
+                if (r >= nr) break;
+                float4 acc;
+                if (pos >= 3) {  // all four taps inside the sequence: one FMA chain per channel
+                    acc.x = __fmul_rn(xr[r].x, wt[0].x);
+                    acc.y = __fmul_rn(xr[r].y, wt[1].x);
+                    acc.z = __fmul_rn(xr[r].z, wt[2].x);
+                    acc.w = __fmul_rn(xr[r].w, wt[3].x);
+#pragma unroll
+                    for (int j = 1; j < 4; ++j) {
+                        acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
+                        acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
+                        acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
+                        acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
+                    }
+                } else {  // the first tokens of a sequence: taps before its start are absent
+                    acc = make_float4(0, 0, 0, 0);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (pos >= 3 - j) {
+                            acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
+                            acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
+                            acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
+                            acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
+                        }
+                    }
+                }
+                finish(r, acc);
+                pos = pos + 1 == period ? 0 : pos + 1;
+            }
         }
         __syncthreads();  // every warp is done with this stage before it is refilled
         stage = (stage + 1) % STAGES;

@@ -448,17 +448,46 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
         bool live[U];
         // every load of the iteration -- inputs, z, and the RoPE table rows
         // (they depend only on the position) -- before any arithmetic
+        // UPW == 1: the warp's U units are consecutive heads; the token and
+        // row pointers of the first come from one division, the rest step
+        // one head at a time (recomputed only where a group or token ends)
+        const int per_tok = a.heads + a.heads2;
+        int hcur = 0;
+        const float* zcur = nullptr;
 #pragma unroll
         for (int k = 0; k < U; ++k) {
             const uint32_t u = base + uint32_t(k * UPW + seg);
             live[k] = u < units;
-            un[k] = head_unit(a, live[k] ? u : 0u, D);
+            if constexpr (UPW == 1) {
+                if (k == 0 || !live[k]) {
+                    un[k] = head_unit(a, live[k] ? u : 0u, D);
+                    hcur = int((live[k] ? u : 0u) - un[k].tok * uint32_t(per_tok));
+                    if constexpr (GATED)
+                        zcur = a.z + int64_t(un[k].tok) * a.z_tok + a.z_off + int64_t(hcur) * a.in_head;
+                } else {
+                    ++hcur;
+                    if (hcur == per_tok || hcur == a.heads) {
+                        un[k] = head_unit(a, u, D);
+                        hcur = int(u - un[k].tok * uint32_t(per_tok));
+                        if constexpr (GATED)
+                            zcur = a.z + int64_t(un[k].tok) * a.z_tok + a.z_off + int64_t(hcur) * a.in_head;
+                    } else {
+                        un[k] = un[k - 1];
+                        un[k].src += un[k].group ? a.in2_head : a.in_head;
+                        un[k].dst += D;
+                        if constexpr (GATED) zcur += a.in_head;
+                    }
+                }
+            } else {
+                un[k] = head_unit(a, live[k] ? u : 0u, D);
+            }
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c)
                 v[k][c] = live[k] ? ld_nc_f4(un[k].src + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);
             if constexpr (GATED) {
-                const float* zs = a.z + int64_t(un[k].tok) * a.z_tok + a.z_off +
-                                  (un[k].src - (a.in + int64_t(un[k].tok) * a.in_tok));
+                const float* zs = UPW == 1 ? zcur
+                                           : a.z + int64_t(un[k].tok) * a.z_tok + a.z_off +
+                                                 (un[k].src - (a.in + int64_t(un[k].tok) * a.in_tok));
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c)
                     zz[k][c] = live[k] ? ld_nc_f4(zs + (c * LPU + l) * 4) : make_float4(0, 0, 0, 0);

@@ -500,11 +500,14 @@ namespace {
 using HeadKernel = void (*)(qdc::HeadArgs);
 
 // Vector head kernel for `dim`, and the units (LPU lanes each) a warp takes
-// per iteration.  Measured on B200 (config-5 shapes): with few units the
-// grid needs more, smaller work items (ramp and tail dominate); with many,
-// two units per warp keep more bytes in flight (+4% for q/k at 65,536
-// tokens, -3% at 8,192).
-constexpr int64_t kManyUnits = 262144;
+// per iteration.  With very few units the grid needs more, smaller work
+// items (ramp and tail dominate); otherwise the wider unroll keeps more
+// bytes in flight.  Since a warp's consecutive units step their row
+// pointers instead of dividing per unit, the wider unroll wins from 81,920
+// units up (measured on B200: q/k +2.4% at 8,192 tokens x 10 heads, +4% at
+// 65,536; gated +0.6% at 8,192 x 16), so only small launches keep the
+// narrow one.
+constexpr int64_t kManyUnits = 32768;
 
 template <bool GATED>
 HeadKernel head_vec_kernel(int dim, int64_t units, int* lpu, int* unroll) {

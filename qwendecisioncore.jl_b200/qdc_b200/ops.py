@@ -17,7 +17,11 @@ for CuArrays and the work done by the library's sm_100a kernels:
                        ext/cuda_attention.jl:92-108
   native_delta_conv_norm  conv + SiLU + q/k L2 norms of delta_attention,
                        src/backbone.jl:287-314, ext/cuda_delta.jl:8-40,122-146
+  native_delta_gates   beta / decay of delta_attention, src/backbone.jl:292-297,
+                       ext/cuda_delta.jl:168-181
   native_mlp_gate      src/backbone.jl:352-355, ext/cuda_mlp.jl:49-61
+  native_bf16_to_f32   BF16 decode (bits << 16), src/safetensors.jl:28-30
+  native_f32_to_bf16   BF16 encode (round to nearest even), src/safetensors.jl:38-42
   rope_table           src/backbone_cpu.jl:90-105
 
 Layout: a Julia (width, tokens) matrix is a (tokens, width) row-major

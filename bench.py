@@ -18,10 +18,13 @@ Metric: whole-job algorithmic HBM bytes per second of those kernels
 with its fraction of the measured HBM roofline.  Time: device CUDA events
 around K replays of a CUDA graph of the step, max over ranks.  Also reported:
 the per-kernel roofline of the dominant kernel (SwiGLU) from an
-event-instrumented replay, the BASELINE per-kernel workloads (configs 2-4),
-an end-to-end number through the C-ABI call with host ids in and the final
-hidden states back on the host, and the CPU oracle's throughput on the
-host cores.
+event-instrumented replay, the BASELINE per-kernel workloads (configs 2-4)
+and the kernels beside the step (DeltaNet prologue, attention gate, BF16
+weight widen and encode) alone over independent input sets, an end-to-end
+number through the C-ABI call with host ids in and the final hidden states
+back on the host (copies overlapped with the next step), the whole
+forward's tokens/s, and the CPU oracle's throughput on the host cores
+(>= 10 s of work).
 
 --impl reference times the reference's own CPU algorithm for the same path
 (the C restatement in oracle/, since the Julia reference cannot run here)

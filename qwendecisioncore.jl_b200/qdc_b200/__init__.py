@@ -15,11 +15,13 @@ from .ops import (Context, context, native_attn_gate, native_bf16_to_f32, native
                   native_q_k_norm_rope, native_qk_norm_rope, native_residual_add_rms,
                   native_residual_rms, native_rms, rope_table)
 
-from .backbone import QwenBackbone, backbone_hidden, backbone_last_hidden, check_sequence
+from .backbone import (QwenBackbone, backbone_hidden, backbone_last_hidden, batch_backbone_hidden,
+                       check_sequence)
 from .model import Config
 
 __all__ = [
-    "QwenBackbone", "backbone_hidden", "backbone_last_hidden", "check_sequence", "Config",
+    "QwenBackbone", "backbone_hidden", "backbone_last_hidden", "batch_backbone_hidden",
+    "check_sequence", "Config",
     "ArgumentError", "DimensionMismatch", "QdcError", "QDC_BF16", "QDC_F32", "Context", "context",
     "declared_symbols", "load", "native_attn_gate", "native_bf16_to_f32", "native_delta_conv_norm",
     "native_delta_gates", "native_f32_to_bf16",

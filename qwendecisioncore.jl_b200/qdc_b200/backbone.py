@@ -5,10 +5,11 @@ Public API, mirroring src/backbone.jl:
   QwenBackbone.from_directory(dir, device)   QwenBackbone(dir; device), :74-192
   backbone_hidden(b, ids, mask[, positions])  :433-460 (host float32 (tokens, hidden))
   backbone_last_hidden(b, ids, mask)          :470-490
+  batch_backbone_hidden(b, ids, mask)         the batched hook of :66-70: each
+                                              row's last-position state, host
+                                              (batch, hidden)
   batch_hidden(b, ids, mask)                  many equal-length sequences in one
-                                              pass (the batched forward the
-                                              reference leaves to accelerators,
-                                              :66-70); device (B*S, hidden)
+                                              pass; device (B*S, hidden)
 
 Per layer (native_layer, src/backbone.jl:363-382):
   input norm   -- qdc gather+norm for layer 0, else fused into the previous
@@ -415,3 +416,35 @@ def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK):
         state = state * final[:, :, c] + corr.transpose(-1, -2) @ ending[:, :, c]
     out = out.view(B, n * chunk, Hv, Dv)
     return out if P == 0 else out[:, :S].contiguous()
+
+
+def sequence_start(mask_row):
+    """native_sequence_start, src/backbone.jl:44-51 (trim_padding on, its
+    default, src/cpu_settings.jl:28): 0-based index of the first unmasked
+    position, or the last position when every position is masked."""
+    nz = np.flatnonzero(np.asarray(mask_row) != 0)
+    return int(nz[0]) if nz.size else len(mask_row) - 1
+
+
+def batch_backbone_hidden(backbone, ids, mask):
+    """The batched hook of src/backbone.jl:66-70, as the reference's Metal
+    extension implements it (ext/metal_batch_forward.jl:104-140): for
+    (batch, seq) ids and mask, the final-normalized hidden state of each
+    row's last position, host float32 (batch, hidden) -- Julia's
+    (hidden, batch), one column per input row.  Leading columns that are
+    masked in every row are dropped first (the earliest sequence_start of
+    the rows); RoPE is relative and fully masked leading tokens add nothing
+    to attention, the DeltaNet state or the conv, so this changes results by
+    rounding only.  All rows go through one last-token forward, replayed as
+    a cached CUDA graph per shape (QDC_B200_GRAPH=0: eagerly)."""
+    ids = np.asarray(ids)
+    mask = np.asarray(mask)
+    if ids.ndim != 2 or mask.shape != ids.shape:
+        raise ArgumentError(1, "batch_backbone_hidden takes (batch, sequence) ids and mask of one shape")
+    for row in range(ids.shape[0]):
+        check_sequence(backbone.config.vocab, ids[row], mask[row])
+    first = min(sequence_start(m) for m in mask)
+    ids, mask = np.ascontiguousarray(ids[:, first:]), np.ascontiguousarray(mask[:, first:])
+    if os.environ.get("QDC_B200_GRAPH", "1") == "0":
+        return backbone.batch_hidden(ids, mask, last_only=True).cpu().numpy()
+    return backbone.last_hidden_graphed(ids, mask)

@@ -215,3 +215,32 @@ def test_safetensors_bf16_decode(tmp_path, oracle):
     raw = read_safetensors(str(path), raw_bf16=True)["w"]
     assert raw.dtype == np.uint16 and raw.shape == (2, 2)
     assert np.array_equal(raw.reshape(-1), bits)
+
+
+def test_batch_backbone_hidden_left_padded_rows(cpu_backbone, monkeypatch):
+    """The batched hook (src/backbone.jl:66-70): each row's last-position
+    state, rows left-padded by different amounts and by a common prefix that
+    is trimmed first (src/backbone.jl:44-51), against the untrimmed
+    single-sequence oracle forward of each row."""
+    import qdc_b200
+    from oracle import forward as F
+    from qdc_b200.model import load_weights
+    monkeypatch.setenv("QDC_B200_GRAPH", "0")
+    cfg, w = load_weights(GOLDEN)
+    model = cpu_backbone(cfg, w)
+    S = 40
+    ids = np.array([(np.arange(S) * (5 + r)) % 64 for r in range(3)])
+    mask = np.ones((3, S), np.int64)
+    for r, pad in enumerate((4, 9, 6)):
+        mask[r, :pad] = 0
+    mask[2, 20] = 0  # a hole inside a row as well
+    out = qdc_b200.batch_backbone_hidden(model, ids, mask)
+    assert out.shape == (3, cfg.hidden)
+    om = F.load_model(GOLDEN)
+    for r in range(3):
+        expected = F.backbone_hidden(om, ids[r], mask[r])[-1]
+        assert np.all(np.abs(out[r] - expected) <= 2e-5 + 2e-5 * np.abs(expected))
+    assert qdc_b200.backbone.sequence_start(mask[0]) == 4
+    assert qdc_b200.backbone.sequence_start(np.zeros(5)) == 4
+    with pytest.raises(qdc_b200.ArgumentError):
+        qdc_b200.batch_backbone_hidden(model, ids, mask[:, :-1])

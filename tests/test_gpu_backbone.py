@@ -296,3 +296,25 @@ def test_delta_keys_64_wide(q):
         expected = F.backbone_hidden(omodel, ids, mask)
         assert _violation(q.backbone_hidden(model, ids, mask).astype(np.float64),
                           expected.astype(np.float64)) <= 1.0
+
+
+def test_batch_backbone_hidden_matches_rows(q, fixture_model, monkeypatch):
+    """The batched hook on the GPU (one graphed last-token forward for all
+    rows) against backbone_last_hidden of each row alone, left padding of
+    different lengths, a common padded prefix trimmed; graph and eager paths
+    agree exactly."""
+    S = 70
+    ids = np.array([(np.arange(S) * (3 + r)) % 64 for r in range(4)])
+    mask = np.ones((4, S), np.int64)
+    for r, pad in enumerate((2, 7, 30, 2)):
+        mask[r, :pad] = 0
+    mask[3, 0:S - 1:3] = 0
+    got = q.batch_backbone_hidden(fixture_model, ids, mask)
+    assert got.shape == (4, fixture_model.config.hidden)
+    for r in range(4):
+        alone = q.backbone_last_hidden(fixture_model, ids[r], mask[r]).astype(np.float64)
+        assert _violation(got[r].astype(np.float64), alone) <= 1.0
+    again = q.batch_backbone_hidden(fixture_model, ids, mask)
+    assert np.array_equal(again, got)
+    monkeypatch.setenv("QDC_B200_GRAPH", "0")
+    assert np.array_equal(q.batch_backbone_hidden(fixture_model, ids, mask), got)

@@ -301,8 +301,8 @@ def test_delta_keys_64_wide(q):
 def test_batch_backbone_hidden_matches_rows(q, fixture_model, monkeypatch):
     """The batched hook on the GPU (one graphed last-token forward for all
     rows) against backbone_last_hidden of each row alone, left padding of
-    different lengths, a common padded prefix trimmed; graph and eager paths
-    agree exactly."""
+    different lengths, a common padded prefix trimmed; replays repeat
+    exactly; the eager path agrees within the bar."""
     S = 70
     ids = np.array([(np.arange(S) * (3 + r)) % 64 for r in range(4)])
     mask = np.ones((4, S), np.int64)
@@ -317,4 +317,5 @@ def test_batch_backbone_hidden_matches_rows(q, fixture_model, monkeypatch):
     again = q.batch_backbone_hidden(fixture_model, ids, mask)
     assert np.array_equal(again, got)
     monkeypatch.setenv("QDC_B200_GRAPH", "0")
-    assert np.array_equal(q.batch_backbone_hidden(fixture_model, ids, mask), got)
+    eager = q.batch_backbone_hidden(fixture_model, ids, mask)
+    assert _violation(eager.astype(np.float64), got.astype(np.float64)) <= 1.0

@@ -15,9 +15,12 @@
 //    issue right after it starts (the kernel boundaries of a short step);
 //  * reductions are warp shuffles; RoPE partners are exchanged by shuffle
 //    instead of being re-read from global (ext/cuda_attention.jl:35);
-//  * Float32 arithmetic uses explicitly rounded intrinsics (__fmul_rn,
-//    __fadd_rn, __fdiv_rn, __fsqrt_rn) in the reference CPU operation order
-//    (src/backbone_cpu.jl), so no multiply-add is contracted;
+//  * elementwise Float32 products and sums use explicitly rounded intrinsics
+//    (__fmul_rn, __fadd_rn, __fsub_rn) in the reference CPU operation order
+//    (src/backbone_cpu.jl), so the compiler contracts none of them; sums of
+//    squares and the conv taps are deliberate FMA chains, and SiLU and the
+//    RMS scale use SFU approximations -- each with its error bound beside
+//    it, all far inside the 1e-6 + 1e-5|b| bar;
 //  * no kernel traps: bad ids set a flag and poison their row with NaN.
 #pragma once
 

@@ -29,6 +29,7 @@ out-of-scope parts; they run as plain torch Float32 ops (cuBLAS GEMMs with
 TF32 disabled, as the reference computes in Float32, src/backbone.jl:14-16).
 """
 
+import collections
 import os
 
 import numpy as np
@@ -40,6 +41,7 @@ from ._lib import ArgumentError
 from .model import Config, device_f32, load_weights, pack_layers, random_weights
 
 FLOATMAX32 = float(np.finfo(np.float32).max)
+MAX_GRAPHS = 32  # cached last-token graphs per model (shapes beyond evict the oldest)
 DELTA_CHUNK = 64  # src/backbone.jl:301, ext/cuda_delta_chunked.jl:9
 
 
@@ -73,7 +75,9 @@ class QwenBackbone:
         self.final_norm = _device_f32(weights["norm.weight"], self.device)
         self.layers = pack_layers(config, weights, self.device)
         self._rope = {}
-        self._graphs = {}  # (B, S, full_mask) -> captured last-token forward
+        # (B, S, full_mask) -> captured last-token forward, least recently
+        # used first; at most MAX_GRAPHS are kept (each holds its own buffers)
+        self._graphs = collections.OrderedDict()
         self.trace = None  # list to record (site, inputs, outputs) of every qdc call
 
     @classmethod
@@ -281,7 +285,10 @@ class QwenBackbone:
         with self.ctx.lock:
             g = self._graphs.get(key)
             if g is None:
+                while len(self._graphs) >= MAX_GRAPHS:
+                    self._graphs.popitem(last=False)
                 g = self._graphs[key] = _GraphedLastHidden(self, *key)
+            self._graphs.move_to_end(key)
             if g.graph is None:
                 return self.batch_hidden(ids, mask, last_only=True).cpu().numpy()
             return g(ids, mask)

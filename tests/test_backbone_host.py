@@ -244,3 +244,30 @@ def test_batch_backbone_hidden_left_padded_rows(cpu_backbone, monkeypatch):
     assert qdc_b200.backbone.sequence_start(np.zeros(5)) == 4
     with pytest.raises(qdc_b200.ArgumentError):
         qdc_b200.batch_backbone_hidden(model, ids, mask[:, :-1])
+
+
+def test_graph_cache_is_bounded(cpu_backbone, monkeypatch):
+    """At most MAX_GRAPHS captured last-token forwards per model, least
+    recently used evicted first (the capture itself is replaced by a stub
+    here: capturing needs a GPU)."""
+    from qdc_b200 import backbone as BB
+    from qdc_b200.model import load_weights
+    made = []
+
+    class Stub:
+        def __init__(self, model, B, S, full):
+            self.graph, self.key = object(), (B, S, full)
+            made.append(self.key)
+
+        def __call__(self, ids, mask):
+            return np.zeros((ids.shape[0], 8), np.float32)
+
+    monkeypatch.setattr(BB, "_GraphedLastHidden", Stub)
+    monkeypatch.setattr(BB, "MAX_GRAPHS", 3)
+    cfg, w = load_weights(GOLDEN)
+    model = cpu_backbone(cfg, w)
+    model._graphs = BB.collections.OrderedDict()
+    for n in (5, 6, 7, 5, 8):
+        model.last_hidden_graphed(np.ones((1, n), np.int64), np.ones((1, n), np.int64))
+    assert list(model._graphs) == [(1, 7, True), (1, 5, True), (1, 8, True)]
+    assert made == [(1, 5, True), (1, 6, True), (1, 7, True), (1, 8, True)]

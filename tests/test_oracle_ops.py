@@ -197,3 +197,72 @@ def test_threads_do_not_change_results(oracle):
     b = oracle.residual_rms(x, m, w, 1e-6)
     oracle.set_threads(1)
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+def _np_delta_conv_norm(proj, w, kh, kd, vh, vd, seq_len, eps=1e-6):
+    """float64 restatement: 4-tap causal conv (taps oldest first, absent
+    before the sequence start), SiLU, per-head L2 norm of q (also / sqrt(kd))
+    and k; v only activated (src/backbone_cpu.jl:787-807, :411-427)."""
+    T = proj.shape[0]
+    C = 2 * kh * kd + vh * vd
+    x = proj[:, :C].astype(np.float64)
+    conv = np.zeros((T, C))
+    for t in range(T):
+        pos = t % seq_len
+        for j in range(4):
+            if pos - 3 + j >= 0:
+                conv[t] += x[t - 3 + j] * w[:, j]
+    s = conv / (1.0 + np.exp(-conv))
+    q = s[:, :kh * kd].reshape(T, kh, kd)
+    k = s[:, kh * kd:2 * kh * kd].reshape(T, kh, kd)
+    v = s[:, 2 * kh * kd:].reshape(T, vh, vd)
+    nq = q / (np.sqrt((q ** 2).sum(-1, keepdims=True) + eps) * np.sqrt(kd))
+    nk = k / np.sqrt((k ** 2).sum(-1, keepdims=True) + eps)
+    return nq, nk, v
+
+
+@pytest.mark.parametrize("tokens,seq_len", [(1, 1), (9, 4), (17, 17), (40, 13)])
+def test_delta_conv_norm_ramps(oracle, tokens, seq_len):
+    kh, kd, vh, vd = 2, 8, 3, 4
+    C = 2 * kh * kd + vh * vd
+    proj = ramp(tokens * (C + 5)).reshape(tokens, C + 5)
+    w = (0.5 * ramp(C * 4, np.cos)).reshape(C, 4)
+    gq, gk, gv = oracle.delta_conv_norm(proj, w, kh, kd, vh, vd, seq_len=seq_len)
+    eq, ek, ev = _np_delta_conv_norm(proj, w.astype(np.float64), kh, kd, vh, vd, seq_len)
+    assert close(gq, eq) and close(gk, ek) and close(gv, ev)
+
+
+def test_delta_conv_norm_edge_values(oracle):
+    """The L2-norm edge values of test/backbone.jl:290-313 after an identity
+    conv (each token its own sequence): exact results."""
+    edges = np.array([0.0, -0.0, np.nan, np.inf, np.finfo(np.float32).max, 1e-45], np.float32)
+    kh, kd, vh, vd = 1, 8, 1, 8
+    C = 2 * kh * kd + vh * vd
+    proj = np.repeat(edges[:, None], C, axis=1)
+    w = np.zeros((C, 4), np.float32)
+    w[:, 3] = 1.0
+    q, k, v = oracle.delta_conv_norm(proj, w, kh, kd, vh, vd, seq_len=1)
+    big = np.finfo(np.float32).max
+    # the conv accumulates into a +0 (value = 0; value += x * w, src/backbone_cpu.jl:
+    # 787-807), so -0 comes out as +0; Inf normalises to inf/inf = NaN, floatmax
+    # to max/inf = 0 (its square overflows the Float32 sum)
+    expect_qk = np.array([0.0, 0.0, np.nan, np.nan, 0.0, 0.0], np.float32)
+    expect_v = np.array([0.0, 0.0, np.nan, np.inf, big, 0.0], np.float32)    # silu only
+    for got, exp in ((q, expect_qk), (k, expect_qk), (v, expect_v)):
+        g = got.reshape(6, -1)
+        for t in range(6):
+            assert np.array_equal(g[t], np.full(g.shape[1], exp[t]), equal_nan=True), (t, g[t])
+            assert np.array_equal(np.signbit(g[t]), np.full(g.shape[1], np.signbit(exp[t])))
+
+
+@pytest.mark.parametrize("B,S,H,D", [(1, 1, 1, 4), (2, 5, 3, 8), (3, 7, 2, 16)])
+def test_attn_gate_ramps(oracle, B, S, H, D):
+    """values .* inv(1 + exp(-gate)), src/backbone.jl:258-259, with the
+    attention output read in (B, H, S, D) and the gate in (B*S, H, D)."""
+    values = ramp(B * H * S * D).reshape(B, H, S, D)
+    packed = (3 * ramp(B * S * H * 2 * D, np.cos)).reshape(B * S, H, 2 * D)
+    gate = packed[:, :, D:]
+    got = oracle.attn_gate(values, np.ascontiguousarray(gate))
+    v = values.astype(np.float64).transpose(0, 2, 1, 3).reshape(B * S, H, D)
+    exp = v / (1.0 + np.exp(-gate.astype(np.float64)))
+    assert close(got.reshape(B * S, H, D), exp)

@@ -252,7 +252,8 @@ def test_delta_conv_norm_edge_values(oracle):
         g = got.reshape(6, -1)
         for t in range(6):
             assert np.array_equal(g[t], np.full(g.shape[1], exp[t]), equal_nan=True), (t, g[t])
-            assert np.array_equal(np.signbit(g[t]), np.full(g.shape[1], np.signbit(exp[t])))
+            if not np.isnan(exp[t]):  # a NaN's sign carries nothing
+                assert np.array_equal(np.signbit(g[t]), np.full(g.shape[1], np.signbit(exp[t])))
 
 
 @pytest.mark.parametrize("B,S,H,D", [(1, 1, 1, 4), (2, 5, 3, 8), (3, 7, 2, 16)])

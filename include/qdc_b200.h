@@ -137,6 +137,14 @@ QDC_API int qdc_gather_rms(qdc_ctx *ctx, void *out_x, void *out_y, const void *t
                    float eps, int centered, int64_t n, int64_t hidden,
                    int64_t vocab, int dtype, void *stream);
 
+/* The plain token-embedding gather, out[t] = table[ids[t]] (bit-exact),
+ * host ids validated and staged as in qdc_gather_rms.  Replaces
+ * native_gather(::CuMatrix, ids) / gather_kernel! (src/backbone.jl:55-64,
+ * ext/cuda_workspace.jl:317-344); the same as qdc_gather_rms with
+ * out_y, add and gamma NULL. */
+QDC_API int qdc_gather(qdc_ctx *ctx, void *out, const void *table, const int32_t *ids,
+                       int64_t n, int64_t hidden, int64_t vocab, int dtype, void *stream);
+
 /* As qdc_gather_rms with DEVICE ids (for graph capture / device-resident
  * batches).  Out-of-range ids are not read: their rows are filled with NaN
  * and the context flag is raised (QDC_EBOUNDS from the next qdc_sync). */

@@ -454,6 +454,13 @@ int qdc_gather_rms_device_ids(qdc_ctx* ctx, void* out_x, void* out_y, const void
     return dtype == QDC_F32 ? launch_rows<float>(ctx, a, stream) : launch_rows<uint16_t>(ctx, a, stream);
 }
 
+int qdc_gather(qdc_ctx* ctx, void* out, const void* table, const int32_t* ids, int64_t n, int64_t hidden,
+               int64_t vocab, int dtype, void* stream) {
+    if (out == nullptr && n > 0) return fail(ctx, QDC_EINVAL, "out is NULL");
+    return qdc_gather_rms(ctx, out, nullptr, table, ids, nullptr, nullptr, 0.0f, 0, n, hidden, vocab, dtype,
+                          stream);
+}
+
 int qdc_gather_rms(qdc_ctx* ctx, void* out_x, void* out_y, const void* table, const int32_t* ids,
                    const void* add, const float* gamma, float eps, int centered, int64_t n,
                    int64_t hidden, int64_t vocab, int dtype, void* stream) {

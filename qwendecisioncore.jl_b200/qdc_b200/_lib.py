@@ -61,6 +61,7 @@ SIGNATURES = {
     "qdc_ws_reset": [_vp],
     "qdc_ws_stats": [_vp, _szp, _szp, _szp],
     "qdc_rope_table": [_flt, _int, _i64, _vp, _vp],
+    "qdc_gather": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "qdc_gather_rms": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _flt, _int, _i64, _i64, _i64, _int, _vp],
     "qdc_gather_rms_device_ids": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _flt, _int, _i64, _i64, _i64,
                                   _int, _vp],

@@ -652,3 +652,27 @@ def test_delta_conv_norm_edge_values(q, oracle, kd, vd):
         assert f32_close(got, exp)
         a = got.cpu().numpy()
         assert np.array_equal(np.isnan(a), np.isnan(exp)) and np.array_equal(np.isinf(a), np.isinf(exp))
+
+
+def test_plain_gather_entry_point(q, oracle):
+    """qdc_gather (the boundary's plain gather): bit-exact rows, host ids
+    checked before launch."""
+    import ctypes
+    from qdc_b200 import _lib, ops
+    ctx = q.context(torch.device("cuda", 0))
+    r = rng(21)
+    V, H, n = 1000, 1024, 77
+    table = r.normal(0, 0.02, (V, H)).astype(np.float32)
+    ids = r.integers(0, V, n).astype(np.int32)
+    out = nan_like((n, H))
+    dt = dev(table)
+    st = ctx.lib.qdc_gather(ctx.handle, ops._ptr(out), ops._ptr(dt), ids.ctypes.data_as(ctypes.c_void_p),
+                            n, H, V, _lib.QDC_F32, ops._stream(torch.device("cuda", 0)))
+    _lib.check(st, ctx.handle)
+    ctx.sync()
+    assert np.array_equal(out.cpu().numpy(), table[ids])
+    bad = ids.copy()
+    bad[5] = V
+    st = ctx.lib.qdc_gather(ctx.handle, ops._ptr(out), ops._ptr(dt), bad.ctypes.data_as(ctypes.c_void_p),
+                            n, H, V, _lib.QDC_F32, ops._stream(torch.device("cuda", 0)))
+    assert st == _lib.QDC_EBOUNDS

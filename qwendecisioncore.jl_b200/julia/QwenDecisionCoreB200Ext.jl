@@ -250,6 +250,93 @@ function upload_bf16(bits::Array{UInt16})
     return out
 end
 
+"""gather!(out, embedding, ids)  -- out[:, t] = embedding[:, ids[t]+1] bit for
+bit (native_gather, src/backbone.jl:55-64); host ids validated and staged."""
+function gather!(out::CUDA.CuMatrix{Float32}, embedding::CUDA.CuMatrix{Float32}, ids::Vector{<:Integer})
+    hidden, vocab = size(embedding)
+    host = Int32.(ids)
+    ctx = context()
+    check(ccall((:qdc_gather, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Int32}, Int64, Int64, Int64, Cint, Ptr{Cvoid}),
+                ctx.handle, ptr(out), ptr(embedding), host, Int64(length(host)), Int64(hidden),
+                Int64(vocab), QDC_F32, stream_handle()), ctx.handle)
+    return out
+end
+
+"""gather_rms_device!(out_x, out_y, embedding, ids, weight, eps)  -- gather_rms!
+with device ids (a CuVector{Int32}, 0-based), for CUDA-graph capture
+(gather_input_kernel!, ext/cuda_io_graph.jl:1-14).  Out-of-range ids poison
+their rows and surface as ArgumentError at the next sync!()."""
+function gather_rms_device!(out_x, out_y, embedding::CUDA.CuMatrix{Float32}, ids::CUDA.CuVector{Int32},
+                            weight, eps)
+    hidden, vocab = size(embedding)
+    ctx = context()
+    check(ccall((:qdc_gather_rms_device_ids, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid},
+                 Cfloat, Cint, Int64, Int64, Int64, Cint, Ptr{Cvoid}),
+                ctx.handle, ptr(out_x), ptr(out_y), ptr(embedding), ptr(ids), C_NULL, ptr(weight),
+                Float32(eps), Cint(1), Int64(length(ids)), Int64(hidden), Int64(vocab), QDC_F32,
+                stream_handle()), ctx.handle)
+    return out_x, out_y
+end
+
+"""q_k_norm_rope!(q, k, projected, q_norm, k_norm, eps, rotary, cos, sin; q_width, k_offset)
+
+The query heads (first dim of each 2dim-wide [q; gate] head) and the key
+heads (rows k_offset .+ (1:dim*kv_heads)) of the packed projection, both
+normalised and rotated in one launch (both prepare_head_kernel! launches of
+ext/cuda_attention.jl:128,141).  q is (dim, heads, tokens), k is
+(dim, kv_heads, tokens)."""
+function q_k_norm_rope!(q::CUDA.CuArray{Float32,3}, k::CUDA.CuArray{Float32,3},
+                        projected::CUDA.CuMatrix{Float32}, q_norm, k_norm, eps, rotary::Integer,
+                        cos::CUDA.CuMatrix{Float32}, sin::CUDA.CuMatrix{Float32}; k_offset::Integer,
+                        seq_len::Integer = 0)
+    dim, heads, tokens = size(q)
+    kv_heads = size(k, 2)
+    ld = Int64(size(projected, 1))
+    ctx = context()
+    check(ccall((:qdc_q_k_norm_rope, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Cint, Cint, Cint,
+                 Int64, Int64, Int64, Int64, Ptr{Cvoid}, Ptr{Cvoid}, Cfloat, Cint, Ptr{Cvoid},
+                 Ptr{Cvoid}, Int64, Int64, Int64, Ptr{Cvoid}),
+                ctx.handle, ptr(q), ptr(k), ptr(projected), ptr(projected) + k_offset * sizeof(Float32),
+                Int64(tokens), Cint(heads), Cint(kv_heads), Cint(dim), ld, Int64(2 * dim), ld,
+                Int64(dim), ptr(q_norm), ptr(k_norm), Float32(eps), Cint(rotary), ptr(cos), ptr(sin),
+                Int64(size(cos, 2)), Int64(0), Int64(seq_len), stream_handle()), ctx.handle)
+    return q, k
+end
+
+"""to_bf16!(out::CuArray{UInt16}, x::CuArray{Float32})  -- bf16 storage of x,
+round to nearest even by integer add (float32_to_bf16, src/safetensors.jl:38-42)."""
+function to_bf16!(out::CUDA.CuArray{UInt16}, x::CUDA.CuArray{Float32})
+    length(out) == length(x) || throw(DimensionMismatch("out and x lengths differ"))
+    ctx = context()
+    check(ccall((:qdc_f32_to_bf16, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Ptr{Cvoid}),
+                ctx.handle, ptr(out), ptr(x), Int64(length(x)), stream_handle()), ctx.handle)
+    return out
+end
+
+"""set_pdl!(on::Bool)  -- QDC_OPT_PDL: programmatic dependent launch for this
+device's context (off by default)."""
+set_pdl!(on::Bool) = check(ccall((:qdc_set_option, LIB), Cint, (Ptr{Cvoid}, Cint, Cint),
+                                 context().handle, Cint(1), Cint(on)), context().handle)
+
+# workspace arena (replaces the slot allocator scratch(T, dims),
+# ext/cuda_workspace.jl:71-87): reserve once, carve per forward, reset.
+ws_reserve!(bytes::Integer) = check(ccall((:qdc_ws_reserve, LIB), Cint, (Ptr{Cvoid}, Csize_t),
+                                          context().handle, Csize_t(bytes)), context().handle)
+ws_reset!() = check(ccall((:qdc_ws_reset, LIB), Cint, (Ptr{Cvoid},), context().handle), context().handle)
+
+"""scratch(T, dims...) -> CuArray{T} carved from the context's arena (not owned:
+valid until the next ws_reset!())."""
+function scratch(::Type{T}, dims::Integer...) where {T}
+    ref = Ref{Ptr{Cvoid}}(C_NULL)
+    ctx = context()
+    check(ccall((:qdc_ws_alloc, LIB), Cint, (Ptr{Cvoid}, Csize_t, Csize_t, Ptr{Ptr{Cvoid}}),
+                ctx.handle, Csize_t(prod(dims) * sizeof(T)), Csize_t(256), ref), ctx.handle)
+    return unsafe_wrap(CUDA.CuArray, CUDA.CuPtr{T}(UInt(ref[])), dims; own = false)
+end
+
 """sync!() -- the synchronize of native_forward_scope's `finally`
 (ext/cuda_workspace.jl:62-66), reporting device-side id errors."""
 sync!() = check(ccall((:qdc_sync, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}), context().handle,
@@ -261,10 +348,13 @@ sync!() = check(ccall((:qdc_sync, LIB), Cint, (Ptr{Cvoid}, Ptr{Cvoid}), context(
 function __init__()
     if use_b200()
         cuda_ext = Base.get_extension(QDC, :QwenDecisionCoreCUDAExt)
-        cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!,
-                                                          qk_norm_rope!, rope_tables, gated_rms!,
+        cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!, gather!,
+                                                          gather_rms_device!, qk_norm_rope!,
+                                                          q_k_norm_rope!, rope_tables, gated_rms!,
                                                           swiglu!, attn_gate!, delta_gates!,
-                                                          delta_conv_norm!, upload_bf16, sync!))
+                                                          delta_conv_norm!, upload_bf16, to_bf16!,
+                                                          set_pdl!, ws_reserve!, ws_reset!,
+                                                          scratch, sync!))
     end
 end
 

@@ -315,7 +315,9 @@ class _GraphedLastHidden:
             # the model's cache replaces them when a longer sequence arrives
             self.rope = model.rope(S)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=self.stream):
+            # thread_local: CUDA calls that other host threads make meanwhile
+            # (outside this model's lock) do not invalidate the capture
+            with torch.cuda.graph(graph, stream=self.stream, capture_error_mode="thread_local"):
                 self._body(model, B, S, full_mask)
             self.graph = graph
         except RuntimeError:

@@ -319,3 +319,32 @@ def test_batch_backbone_hidden_matches_rows(q, fixture_model, monkeypatch):
     monkeypatch.setenv("QDC_B200_GRAPH", "0")
     eager = q.batch_backbone_hidden(fixture_model, ids, mask)
     assert _violation(eager.astype(np.float64), got.astype(np.float64)) <= 1.0
+
+
+def test_capture_survives_other_threads_cuda_work(q):
+    """A last-token graph captured while another host thread keeps running
+    unrelated CUDA work (thread-local capture mode) is valid and exact."""
+    import threading
+    model = q.QwenBackbone.from_directory(GOLDEN, device="cuda")
+    ids = (np.arange(23) * 7) % 64
+    mask = np.ones(23, np.int64)
+    expected = q.backbone_hidden(model, ids, mask)[-1]
+    stop = threading.Event()
+
+    def busy():
+        s = torch.cuda.Stream()
+        a = torch.randn(512, 512, device="cuda")
+        with torch.cuda.stream(s):
+            while not stop.is_set():
+                a = torch.tanh(a @ a.t() * 1e-3)
+                s.synchronize()
+
+    t = threading.Thread(target=busy)
+    t.start()
+    try:
+        got = q.backbone_last_hidden(model, ids, mask)   # captures the graph now
+    finally:
+        stop.set()
+        t.join(timeout=60)
+    assert model._graphs[(1, 23, True)].graph is not None
+    assert _violation(got.astype(np.float64), expected.astype(np.float64)) <= 1.0

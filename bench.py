@@ -477,6 +477,45 @@ def config5():
                       "linear_attention" if k == "delta" else "full_attention" for k in KINDS])
 
 
+# The reference's own inference benchmark (benchmark/inference.jl on the
+# synthetic backbone of benchmark/synthetic.jl:4-30): backbone_last_hidden,
+# ids 0:n-1 mod 256, full mask, 3 warm-up calls, median of 21 wall-clock calls
+# per length.  Its published medians (RTX 3060, CUDA.jl; benchmark/results/
+# inference-next-15-2026-10-24.txt:67-74) are quoted beside ours as context:
+# other hardware, same workload and API.
+REFERENCE_INFERENCE_MS = {64: 0.845, 128: 0.975, 256: 1.423, 512: 2.284}
+
+
+def inference_latency(device, samples=21):
+    import statistics
+    import numpy as np
+    import qdc_b200 as q
+    from qdc_b200.model import Config
+    cfg = Config(hidden=256, head_dim=64, heads=4, kv_heads=2, key_heads=2, value_heads=4, key_dim=128,
+                 value_dim=128, eps=float(np.float32(1e-6)), rope_theta=10000.0, rotary_dim=16, vocab=256,
+                 intermediate=512, layer_types=["linear_attention"] * 3 + ["full_attention"])
+    model = q.QwenBackbone.random(cfg, seed=42, device=device)
+    medians = {}
+    for n in REFERENCE_INFERENCE_MS:
+        ids = np.arange(n) % 256
+        mask = np.ones(n, np.int64)
+        for _ in range(4):  # the first call captures the graph; then 3 warm-up calls
+            q.backbone_last_hidden(model, ids, mask)
+        times = []
+        for _ in range(samples):
+            t0 = time.perf_counter()
+            q.backbone_last_hidden(model, ids, mask)
+            times.append(time.perf_counter() - t0)
+        medians[n] = round(statistics.median(times) * 1e3, 4)
+    return {"median_ms": medians, "aggregate_ms": round(sum(medians.values()), 4),
+            "reference_rtx3060_median_ms": REFERENCE_INFERENCE_MS,
+            "reference_rtx3060_aggregate_ms": round(sum(REFERENCE_INFERENCE_MS.values()), 3),
+            "what": "backbone_last_hidden wall clock (host ids in, host vector out) on the reference's "
+                    "synthetic 4-layer hybrid (hidden 256, Delta 2x128 / 4x128, 4/2 heads x 64), "
+                    f"median of {samples} calls after 3 warm-up calls per length; the reference's "
+                    "numbers are its published RTX 3060 medians for the same workload"}
+
+
 def forward_leg(world, rank, device, seqs, steps, warmup, max_over_ranks):
     """Forward tokens/sec of the whole config-5 forward (random-init weights,
     Float32): the rank's sequences through QwenBackbone.batch_hidden, every
@@ -807,6 +846,11 @@ def main():
     if rank == 0 and not args.no_configs:
         configs = kernel_configs(device, peak)
 
+    # --- the reference's own inference benchmark (rank 0 at N=1) ------------
+    latency = None
+    if rank == 0 and world == 1 and not args.no_forward:
+        latency = inference_latency(device)
+
     # --- CPU baseline (rank 0 at N=1) -------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -872,6 +916,8 @@ def main():
         }
         if forward is not None:
             line["forward"] = forward
+        if latency is not None:
+            line["inference_latency"] = latency
         if configs is not None:
             line["configs"] = configs
         if cpu is not None:

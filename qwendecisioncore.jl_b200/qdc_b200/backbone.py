@@ -375,7 +375,10 @@ def backbone_last_hidden(backbone, ids, mask):
     return backbone.last_hidden_graphed(ids, mask)[0]
 
 
-def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK):
+SCAN_MAX_HEADS = 64  # batch x value heads up to which the hand-off runs as a linear scan
+
+
+def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK, scan=None):
     """Gated delta rule in 64-token chunks (src/backbone.jl:309-343), batched
     over sequences, value heads and chunks; only the state hand-off between
     chunks is sequential.
@@ -383,7 +386,12 @@ def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK):
     q, k: (B, S, Hk, Dk) normalised; v: (B, S, Hv, Dv); beta, decay: (B, S, Hv).
     Returns o: (B, S, Hv, Dv).  A short last chunk is zero-padded: padded
     tokens have beta = 0, k = q = v = 0 and decay 0, so they change neither
-    the real tokens' outputs nor the carried state."""
+    the real tokens' outputs nor the carried state.
+
+    `scan` picks how the hand-off runs: as a linear recurrence in the state,
+    one batched multiply-add per chunk (few launches: latency-bound calls,
+    batch x value heads <= SCAN_MAX_HEADS by default), or per chunk in the
+    correction form (about half the arithmetic: throughput-bound calls)."""
     B, S, Hk, Dk = q.shape
     Hv, Dv = v.shape[2], v.shape[3]
     n = (S + chunk - 1) // chunk
@@ -413,16 +421,41 @@ def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK):
     intra_t = (Q @ K.transpose(-1, -2)) * pair                                  # [j, i] = q_j k_i pair[j,i]
     qe = Q * e
     end = cum[..., -1:]
-    ending = K * torch.exp(end - cum)[..., None]
-    final = torch.exp(end)[..., None]                                           # (B,H,n,1,1)
-    state = torch.zeros((B, Hv, Dv, Dk), dtype=q.dtype, device=q.device)
+    ending = K * torch.exp(end - cum)[..., None]                                # E_c: (B,H,n,C,Dk)
+    final = torch.exp(end)[..., None]                                           # f_c: (B,H,n,1,1)
+    if scan is None:
+        scan = B * Hv <= SCAN_MAX_HEADS
+    if not scan:
+        state = torch.zeros((B, Hv, Dv, Dk), dtype=q.dtype, device=q.device)
+        out = torch.empty((B, n, chunk, Hv, Dv), dtype=q.dtype, device=q.device)
+        for c in range(n):
+            corr = new_values[:, :, c] - reading[:, :, c] @ state.transpose(-1, -2)  # (B,H,C,Dv)
+            out[:, c] = (qe[:, :, c] @ state.transpose(-1, -2) + intra_t[:, :, c] @ corr).transpose(1, 2)
+            state = state * final[:, :, c] + corr.transpose(-1, -2) @ ending[:, :, c]
+        out = out.view(B, n * chunk, Hv, Dv)
+        return out if P == 0 else out[:, :S].contiguous()
+    # The hand-off is linear in the state S (Dv x Dk): with the chunk's
+    # correction corr = new_values - reading @ S^T,
+    #   S_c   = S_{c-1} f_c + corr^T E_c = S_{c-1} A_c + B_c,
+    #           A_c = f_c I - reading^T E_c,  B_c = new_values^T E_c;
+    #   out_c = qe S^T + intra corr = W_c S_{c-1}^T + U_c,
+    #           W_c = qe - intra @ reading,   U_c = intra @ new_values.
+    # A, B, W, U are batched over every chunk; the loop is one multiply-add
+    # per chunk, and the outputs are one batched product afterwards.
+    eye = torch.eye(Dk, dtype=q.dtype, device=q.device)
+    chunk_major = lambda t: t.permute(2, 0, 1, 3, 4).reshape(n, B * Hv, t.shape[-2], t.shape[-1])
+    A = chunk_major(final * eye - reading.transpose(-1, -2) @ ending)           # (n,BH,Dk,Dk)
+    Bc = chunk_major(new_values.transpose(-1, -2) @ ending)                     # (n,BH,Dv,Dk)
+    W = qe - intra_t @ reading                                                  # (B,H,n,C,Dk)
+    U = intra_t @ new_values                                                    # (B,H,n,C,Dv)
+    states = torch.empty((n + 1, B * Hv, Dv, Dk), dtype=q.dtype, device=q.device)  # S_0 .. S_n
+    states[0].zero_()
+    for c in range(n):
+        torch.baddbmm(Bc[c], states[c], A[c], out=states[c + 1])
+    before = states[:n].view(n, B, Hv, Dv, Dk).permute(1, 2, 0, 3, 4)            # S_{c-1}: (B,H,n,Dv,Dk)
     # token-major output, heads contiguous within a token (the layout the
     # gated norm reads)
-    out = torch.empty((B, n, chunk, Hv, Dv), dtype=q.dtype, device=q.device)
-    for c in range(n):
-        corr = new_values[:, :, c] - reading[:, :, c] @ state.transpose(-1, -2)  # (B,H,C,Dv)
-        out[:, c] = (qe[:, :, c] @ state.transpose(-1, -2) + intra_t[:, :, c] @ corr).transpose(1, 2)
-        state = state * final[:, :, c] + corr.transpose(-1, -2) @ ending[:, :, c]
+    out = (W @ before.transpose(-1, -2) + U).permute(0, 2, 3, 1, 4).contiguous()  # (B,n,C,H,Dv)
     out = out.view(B, n * chunk, Hv, Dv)
     return out if P == 0 else out[:, :S].contiguous()
 

@@ -143,9 +143,11 @@ def test_last_token_forward_orchestration(cpu_backbone, n, holes):
     assert np.all(np.abs(last - full) <= 2e-5 + 2e-5 * np.abs(full))
 
 
-def test_chunked_delta_matches_token_recurrence():
-    """The chunked rule (zero-padded tail chunk) equals the token recurrence
-    of src/backbone_cpu.jl:681-705 on odd lengths."""
+@pytest.mark.parametrize("scan", [True, False])
+def test_chunked_delta_matches_token_recurrence(scan):
+    """The chunked rule (zero-padded tail chunk), with the hand-off as a
+    linear scan and per chunk, equals the token recurrence of
+    src/backbone_cpu.jl:681-705 on odd lengths."""
     from qdc_b200.backbone import chunked_delta
     g = torch.Generator().manual_seed(0)
     for S in (1, 63, 64, 65, 130):
@@ -155,7 +157,7 @@ def test_chunked_delta_matches_token_recurrence():
         v = torch.randn(B, S, Hv, Dv, generator=g)
         beta = torch.rand(B, S, Hv, generator=g)
         decay = -torch.rand(B, S, Hv, generator=g)
-        out = chunked_delta(q, k, v, beta, decay, Hv // Hk).double()
+        out = chunked_delta(q, k, v, beta, decay, Hv // Hk, scan=scan).double()
         for b in range(B):
             for h in range(Hv):
                 kh = h // (Hv // Hk)

@@ -348,3 +348,26 @@ def test_capture_survives_other_threads_cuda_work(q):
         t.join(timeout=60)
     assert model._graphs[(1, 23, True)].graph is not None
     assert _violation(got.astype(np.float64), expected.astype(np.float64)) <= 1.0
+
+
+@pytest.mark.parametrize("B,S,Hk,Hv", [(1, 130, 2, 4), (4, 256, 4, 16), (8, 65, 2, 8)])
+def test_chunked_delta_forms_agree_on_gpu(B, S, Hk, Hv):
+    """The two hand-off forms of the chunked delta rule (linear scan and per
+    chunk) give the same outputs on the GPU."""
+    from qdc_b200.backbone import chunked_delta
+    g = torch.Generator(device="cuda").manual_seed(B * S + Hv)
+    Dk, Dv = 128, 128
+    kw = dict(device="cuda", generator=g)
+    q = torch.nn.functional.normalize(torch.randn(B, S, Hk, Dk, **kw), dim=-1) / Dk ** 0.5
+    k = torch.nn.functional.normalize(torch.randn(B, S, Hk, Dk, **kw), dim=-1)
+    v = torch.randn(B, S, Hv, Dv, **kw)
+    beta = torch.rand(B, S, Hv, **kw)
+    decay = -torch.rand(B, S, Hv, **kw)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        a = chunked_delta(q, k, v, beta, decay, Hv // Hk, scan=True).double()
+        b = chunked_delta(q, k, v, beta, decay, Hv // Hk, scan=False).double()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert torch.all((a - b).abs() <= TOL + TOL * b.abs())

@@ -175,11 +175,12 @@ class QwenBackbone:
         self._record("attn_gate", (out, qgate[:, :, D:]), (gated,))
         return gated @ layer["out"].t()
 
-    def _delta_attention(self, layer, y, mask, B, S):
+    def _delta_attention(self, layer, y, mask, B, S, full_mask=False):
         cfg = self.config
         T = B * S
         kw, vw, C = cfg.key_width, cfg.value_width, cfg.qkv_width
-        masked = y * mask.view(T, 1).to(torch.float32)
+        # masked tokens enter the DeltaNet as zeros (src/backbone.jl:286)
+        masked = y if full_mask else y * mask.view(T, 1).to(torch.float32)
         proj = masked @ layer["proj"].t()  # [qkv | z | a | b] per token
         # causal 4-tap conv + SiLU + q/k L2 norms in one qdc pass over the
         # projection (src/backbone.jl:287-314)
@@ -229,12 +230,12 @@ class QwenBackbone:
                     if layer["kind"] == "full":
                         mixed = self._full_attention_last(layer, y, mask, B, S, full_mask)
                     else:
-                        mixed = rows(self._delta_attention(layer, y, mask, B, S))
+                        mixed = rows(self._delta_attention(layer, y, mask, B, S, full_mask))
                     x = rows(x)
                 elif layer["kind"] == "full":
                     mixed = self._full_attention(layer, y, mask, B, S, full_mask)
                 else:
-                    mixed = self._delta_attention(layer, y, mask, B, S)
+                    mixed = self._delta_attention(layer, y, mask, B, S, full_mask)
                 r, y = ops.native_residual_rms(x, mixed, layer["post_norm"], cfg.eps, ctx=self.ctx)
                 self._record("post_rms", (x, mixed), (r, y))
                 gu = y @ layer["gate_up"].t()
@@ -399,25 +400,32 @@ def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK, scan=None):
     idx = torch.arange(Hv, device=q.device) // groups  # kv head of value head h: cld(h, groups)
 
     def per_head(t, heads_idx=None):  # (B, S, H, D) -> (B, H, n, C, D)
-        if heads_idx is not None:
+        if heads_idx is not None and groups > 1:
             t = t[:, :, heads_idx]
-        t = F.pad(t, (0, 0, 0, 0, 0, P))
+        if P:
+            t = F.pad(t, (0, 0, 0, 0, 0, P))
         return t.view(B, n, chunk, t.shape[2], t.shape[3]).permute(0, 3, 1, 2, 4)
 
+    def per_head_scalar(t):  # (B, S, H) -> (B, H, n, C)
+        if P:
+            t = F.pad(t, (0, 0, 0, P))
+        return t.view(B, n, chunk, Hv).permute(0, 3, 1, 2)
+
     Q, K, V = per_head(q, idx), per_head(k, idx), per_head(v)
-    bet = F.pad(beta, (0, 0, 0, P)).view(B, n, chunk, Hv).permute(0, 3, 1, 2)   # (B,H,n,C)
-    g = F.pad(decay, (0, 0, 0, P)).view(B, n, chunk, Hv).permute(0, 3, 1, 2)
-    cum = torch.cumsum(g, dim=-1)
-    lower = torch.ones((chunk, chunk), dtype=torch.bool, device=q.device).tril()
+    bet = per_head_scalar(beta)
+    cum = torch.cumsum(per_head_scalar(decay), dim=-1)
+    upper = torch.ones((chunk, chunk), dtype=torch.bool, device=q.device).triu(1)
     diff = cum[..., :, None] - cum[..., None, :]
-    pair = torch.where(lower, torch.exp(torch.where(lower, diff, torch.zeros_like(diff))),
-                       torch.zeros_like(diff))                                 # (B,H,n,C,C)
+    # exp(cum_j - cum_i) on and below the diagonal, 0 above (never exp of a positive gap)
+    pair = torch.exp(diff.masked_fill_(upper, float("-inf")))                  # (B,H,n,C,C)
     kb = K * bet[..., None]
     system = (kb @ K.transpose(-1, -2)) * pair
     L = torch.tril(system, diagonal=-1) + torch.eye(chunk, device=q.device)
     e = torch.exp(cum)[..., None]
-    new_values = torch.linalg.solve_triangular(L, V * bet[..., None], upper=False, unitriangular=True)
-    reading = torch.linalg.solve_triangular(L, kb * e, upper=False, unitriangular=True)
+    # one unit-lower-triangular solve for both right-hand sides
+    both = torch.linalg.solve_triangular(L, torch.cat([V * bet[..., None], kb * e], dim=-1),
+                                         upper=False, unitriangular=True)
+    new_values, reading = both[..., :Dv], both[..., Dv:]
     intra_t = (Q @ K.transpose(-1, -2)) * pair                                  # [j, i] = q_j k_i pair[j,i]
     qe = Q * e
     end = cum[..., -1:]

@@ -1,6 +1,6 @@
 """Build libqdc_b200.so (sm_100a) in-tree with nvcc.
 
-    python qwendecisioncore.jl_b200/build.py [--debug]
+    python qwendecisioncore.jl_b200/build.py
 
 Output: qwendecisioncore.jl_b200/_build/libqdc_b200.so.  The library is a
 plain C ABI (include/qdc_b200.h) linked against the CUDA runtime only; it
@@ -34,7 +34,7 @@ def needs_build():
     return any(os.path.getmtime(p) > t for p in DEPS)
 
 
-def build(force=False, debug=False):
+def build(force=False):
     if not force and not needs_build():
         return LIB
     os.makedirs(OUT_DIR, exist_ok=True)
@@ -43,8 +43,6 @@ def build(force=False, debug=False):
            "-Xptxas", "-v", "--expt-relaxed-constexpr",
            "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(HERE, "csrc"),
            "-DQDC_B200_BUILD", "-o", LIB] + SOURCES + ["-lcudart"]
-    if debug:
-        cmd.insert(1, "-DQDC_DEBUG")
     res = subprocess.run(cmd, capture_output=True, text=True)
     with open(os.path.join(OUT_DIR, "ptxas.txt"), "w") as f:
         f.write(res.stdout + res.stderr)
@@ -57,4 +55,4 @@ def build(force=False, debug=False):
 
 
 if __name__ == "__main__":
-    print(build(force=True, debug="--debug" in sys.argv))
+    print(build(force=True))

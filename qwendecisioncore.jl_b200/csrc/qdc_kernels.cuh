@@ -840,14 +840,16 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         };
         if (nr == TPW && pos0 >= 3 && pos0 + TPW <= period) {
             // the common case: every token of the run has all four taps inside
-            // its sequence -- one FMA chain per channel, no per-token branch
+            // its sequence -- one FMA chain per channel, no per-token branch.
+            // The chain starts as fma(x, w, +0), like the reference's
+            // `value = 0; value += x * w`, so a -0 product gives +0.
 #pragma unroll
             for (int r = 0; r < TPW; ++r) {
                 float4 acc;
-                acc.x = __fmul_rn(xr[r].x, wt[0].x);
-                acc.y = __fmul_rn(xr[r].y, wt[1].x);
-                acc.z = __fmul_rn(xr[r].z, wt[2].x);
-                acc.w = __fmul_rn(xr[r].w, wt[3].x);
+                acc.x = __fmaf_rn(xr[r].x, wt[0].x, 0.0f);
+                acc.y = __fmaf_rn(xr[r].y, wt[1].x, 0.0f);
+                acc.z = __fmaf_rn(xr[r].z, wt[2].x, 0.0f);
+                acc.w = __fmaf_rn(xr[r].w, wt[3].x, 0.0f);
 #pragma unroll
                 for (int j = 1; j < 4; ++j) {
                     acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
@@ -864,10 +866,10 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
                 if (r >= nr) break;
                 float4 acc;
                 if (pos >= 3) {  // all four taps inside the sequence: one FMA chain per channel
-                    acc.x = __fmul_rn(xr[r].x, wt[0].x);
-                    acc.y = __fmul_rn(xr[r].y, wt[1].x);
-                    acc.z = __fmul_rn(xr[r].z, wt[2].x);
-                    acc.w = __fmul_rn(xr[r].w, wt[3].x);
+                    acc.x = __fmaf_rn(xr[r].x, wt[0].x, 0.0f);
+                    acc.y = __fmaf_rn(xr[r].y, wt[1].x, 0.0f);
+                    acc.z = __fmaf_rn(xr[r].z, wt[2].x, 0.0f);
+                    acc.w = __fmaf_rn(xr[r].w, wt[3].x, 0.0f);
 #pragma unroll
                     for (int j = 1; j < 4; ++j) {
                         acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);

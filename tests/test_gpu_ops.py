@@ -676,3 +676,19 @@ def test_plain_gather_entry_point(q, oracle):
     st = ctx.lib.qdc_gather(ctx.handle, ops._ptr(out), ops._ptr(dt), bad.ctypes.data_as(ctypes.c_void_p),
                             n, H, V, _lib.QDC_F32, ops._stream(torch.device("cuda", 0)))
     assert st == _lib.QDC_EBOUNDS
+
+
+def test_delta_conv_norm_negative_zero_window(q, oracle):
+    """All taps -0 inside one long sequence (the pipeline's branch-free path):
+    the conv starts from +0 as the reference's `value = 0; value += x * w`
+    does, so every output is +0, sign included."""
+    kh, kd, vh, vd, tokens = 2, 128, 4, 128, 200
+    C = 2 * kh * kd + vh * vd
+    proj = np.full((tokens, C), -0.0, np.float32)
+    w = rng(4).normal(0, 0.5, (C, 4)).astype(np.float32)
+    eq, ek, ev = oracle.delta_conv_norm(proj, w, kh, kd, vh, vd, seq_len=None)
+    gq, gk, gv = q.native_delta_conv_norm(dev(proj), dev(w), kh, kd, vh, vd)
+    for got, exp in ((gq, eq), (gk, ek), (gv, ev)):
+        a = got.cpu().numpy()
+        assert np.array_equal(a, exp) and np.array_equal(np.signbit(a), np.signbit(exp))
+        assert not np.signbit(exp).any()

@@ -19,6 +19,20 @@ from conftest import GOLDEN
 TOL = 2e-5  # test/backbone.jl:10,24
 
 
+def test_fixtures_match_manifest():
+    """The committed fixtures are byte-for-byte the reference's
+    (test/fixtures/native, SHA-256 recorded by tests/golden/make_golden.py)."""
+    import hashlib
+    with open(os.path.join(GOLDEN, "MANIFEST.json")) as f:
+        manifest = json.load(f)
+    files = [k for k in manifest if not k.startswith("_")]
+    assert set(files) == {"config.json", "model.safetensors", "readout.safetensors", "reference.json",
+                          "cuda_reference.json"}
+    for name in files:
+        with open(os.path.join(GOLDEN, name), "rb") as f:
+            assert hashlib.sha256(f.read()).hexdigest() == manifest[name], name
+
+
 @pytest.fixture(scope="module")
 def model(oracle):
     from oracle import forward as F

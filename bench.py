@@ -842,8 +842,10 @@ def main():
                            "weights; device-event time, max over ranks"}
 
     # --- BASELINE per-kernel configs (rank 0 GPU) -------------------------
+    # single-GPU characteristics of each kernel: measured at N=1 only (at
+    # N>1 the other ranks would only wait for them)
     configs = None
-    if rank == 0 and not args.no_configs:
+    if rank == 0 and world == 1 and not args.no_configs:
         configs = kernel_configs(device, peak)
 
     # --- the reference's own inference benchmark (rank 0 at N=1) ------------

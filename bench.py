@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 A step is one pass of the hot path over one batch: the full-depth
-0.8B-shaped layer-kernel sequence -- gather + input norm,
+0.8B-shaped layer-kernel sequence (24 layers, hidden 1024) -- gather + input norm,
 then per layer (pattern [GDN, GDN, GDN, full] x 6) the gated norm or the q/k
 norm + partial RoPE, the post-attention residual norm, SwiGLU, and the MLP
 residual add fused with the next input norm (the final norm after the last
@@ -18,7 +18,8 @@ Metric: whole-job algorithmic HBM bytes per second of those kernels
 with its fraction of the measured HBM roofline.  Time: device CUDA events
 around K replays of a CUDA graph of the step, max over ranks.  Also reported:
 the per-kernel roofline of the dominant kernel (SwiGLU) from an
-event-instrumented replay, the BASELINE per-kernel workloads (configs 2-4)
+event-instrumented replay, the single-kernel workloads (gather + residual norm at
+16,384 tokens, q/k norm + RoPE, residual norm and SwiGLU at 32,768 rows)
 and the kernels beside the step (DeltaNet prologue, attention gate, BF16
 weight widen and encode) alone over independent input sets, an end-to-end
 number through the C-ABI call with host ids in and the final hidden states
@@ -49,7 +50,7 @@ METRIC = "fused layer-kernel HBM GB/s (% of roofline) and forward tokens/sec at 
 FALLBACK_HBM_GBS = 6650.0
 SPEC_HBM_GBS = 8000.0  # B200 HBM3e data-sheet bandwidth (DGX figure)
 
-# BASELINE config 5 (0.8B-shaped): hidden 1024, intermediate 3584, 24 layers.
+# The 0.8B-shaped hybrid backbone: hidden 1024, intermediate 3584, 24 layers.
 HIDDEN, INTER, LAYERS = 1024, 3584, 24
 HQ, HKV, HEAD_DIM, ROTARY, THETA = 8, 2, 256, 64, 1e7
 HK, DK, HV, DV = 16, 128, 16, 128
@@ -252,7 +253,7 @@ class LayerKernelStep:
 # ------------------------------------------------------ per-kernel configs
 
 def single_kernel(name, tokens, device, seed=1):
-    """One per-layer kernel on BASELINE-shaped inputs of `tokens` rows.
+    """One per-layer kernel on inputs of the 0.8B-shaped backbone, `tokens` rows.
     Returns (launch function, algorithmic bytes per launch)."""
     import torch
     import qdc_b200 as q
@@ -412,7 +413,7 @@ def time_launches(fns, device, reps, warmup=3, repeats=21):
     return times[len(times) // 2]
 
 
-CONFIG_CASES = [  # (report name, kernel, tokens)
+CONFIG_CASES = [  # (report name, kernel, tokens): the single-kernel workloads
     ("cfg2_gather_residual_rms_f32", "gather_rms", 16384),
     ("cfg2_gather_residual_rms_bf16", "gather_rms_bf16", 16384),
     ("cfg3_qk_norm_rope", "qk_norm_rope", 16384),
@@ -432,7 +433,7 @@ CONFIG_CASES = [  # (report name, kernel, tokens)
 
 
 def kernel_configs(device, peak, reps=50):
-    """BASELINE configs 2-4 as single-kernel workloads: GB/s and fraction of
+    """The single-kernel workloads: GB/s and fraction of
     the HBM peak, each averaged over `reps` back-to-back launches that cycle
     over independent input sets, >= 3 x L2 touched before a set is reused."""
     import torch
@@ -469,7 +470,7 @@ def run_single_kernel(args):
 # ------------------------------------------------------------- forward leg
 
 def config5():
-    """the 0.8B-shaped hybrid backbone."""
+    """The 0.8B-shaped hybrid backbone: 24 layers [GDN, GDN, GDN, full] x 6."""
     from qdc_b200.model import Config
     return Config(hidden=HIDDEN, head_dim=HEAD_DIM, heads=HQ, kv_heads=HKV, key_heads=HK,
                   value_heads=HV, key_dim=DK, value_dim=DV, eps=float(EPS), rope_theta=THETA,
@@ -841,7 +842,7 @@ def main():
                            "chunked gated delta rule as the out-of-scope stand-ins; random-init "
                            "weights; device-event time, max over ranks"}
 
-    # --- BASELINE per-kernel configs (rank 0 GPU) -------------------------
+    # --- single-kernel workloads (rank 0 GPU) ----------------------------
     # single-GPU characteristics of each kernel: measured at N=1 only (at
     # N>1 the other ranks would only wait for them)
     configs = None

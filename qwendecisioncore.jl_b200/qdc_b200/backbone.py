@@ -469,32 +469,47 @@ def chunked_delta(q, k, v, beta, decay, groups, chunk=DELTA_CHUNK, scan=None):
 
 
 def sequence_start(mask_row):
-    """native_sequence_start, src/backbone.jl:44-51 (trim_padding on, its
-    default, src/cpu_settings.jl:28): 0-based index of the first unmasked
-    position, or the last position when every position is masked."""
+    """native_sequence_start with trimming on (src/backbone.jl:44-51): the
+    0-based index of the first unmasked position, or the last position when
+    every position is masked."""
     nz = np.flatnonzero(np.asarray(mask_row) != 0)
     return int(nz[0]) if nz.size else len(mask_row) - 1
 
 
-def batch_backbone_hidden(backbone, ids, mask):
+def trim_padding_enabled():
+    """The CUDA extension's padding switch (ext/QwenDecisionCoreCUDAExt.jl:
+    12-20): complete sequences are kept unless QDC_B200_TRIM_PADDING=1 (the
+    reference's QDC_CUDA_TRIM_PADDING), so timings compare like for like."""
+    return os.environ.get("QDC_B200_TRIM_PADDING", "0") == "1"
+
+
+def batch_backbone_hidden(backbone, ids, mask, trim_padding=None):
     """The batched hook of src/backbone.jl:66-70, as the reference's Metal
     extension implements it (ext/metal_batch_forward.jl:104-140): for
     (batch, seq) ids and mask, the final-normalized hidden state of each
     row's last position, host float32 (batch, hidden) -- Julia's
-    (hidden, batch), one column per input row.  Leading columns that are
-    masked in every row are dropped first (the earliest sequence_start of
-    the rows); RoPE is relative and fully masked leading tokens add nothing
-    to attention, the DeltaNet state or the conv, so this changes results by
-    rounding only.  All rows go through one last-token forward, replayed as
-    a cached CUDA graph per shape (QDC_B200_GRAPH=0: eagerly)."""
+    (hidden, batch), one column per input row.
+
+    Padding: like the reference's CUDA extension, complete sequences are
+    kept by default (ext/QwenDecisionCoreCUDAExt.jl:12-20).  With
+    `trim_padding=True` (or, when it is None, QDC_B200_TRIM_PADDING=1) the
+    leading columns that are masked in every row are dropped first (the
+    earliest native_sequence_start of the rows, src/backbone.jl:44-51); RoPE
+    is relative and fully masked leading tokens add nothing to attention,
+    the DeltaNet state or the conv, so trimming changes results by rounding
+    only.  All rows go through one last-token forward, replayed as a cached
+    CUDA graph per shape (QDC_B200_GRAPH=0: eagerly)."""
     ids = np.asarray(ids)
     mask = np.asarray(mask)
     if ids.ndim != 2 or mask.shape != ids.shape:
         raise ArgumentError(1, "batch_backbone_hidden takes (batch, sequence) ids and mask of one shape")
     for row in range(ids.shape[0]):
         check_sequence(backbone.config.vocab, ids[row], mask[row])
-    first = min(sequence_start(m) for m in mask)
-    ids, mask = np.ascontiguousarray(ids[:, first:]), np.ascontiguousarray(mask[:, first:])
+    if trim_padding is None:
+        trim_padding = trim_padding_enabled()
+    if trim_padding:
+        first = min(sequence_start(m) for m in mask)
+        ids, mask = np.ascontiguousarray(ids[:, first:]), np.ascontiguousarray(mask[:, first:])
     if os.environ.get("QDC_B200_GRAPH", "1") == "0":
         return backbone.batch_hidden(ids, mask, last_only=True).cpu().numpy()
     return backbone.last_hidden_graphed(ids, mask)

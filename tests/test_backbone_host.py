@@ -219,25 +219,41 @@ def test_safetensors_bf16_decode(tmp_path, oracle):
     assert np.array_equal(raw.reshape(-1), bits)
 
 
-def test_batch_backbone_hidden_left_padded_rows(cpu_backbone, monkeypatch):
+@pytest.mark.parametrize("trim", [None, False, True, "env"])
+def test_batch_backbone_hidden_left_padded_rows(cpu_backbone, monkeypatch, trim):
     """The batched hook (src/backbone.jl:66-70): each row's last-position
-    state, rows left-padded by different amounts and by a common prefix that
-    is trimmed first (src/backbone.jl:44-51), against the untrimmed
-    single-sequence oracle forward of each row."""
+    state, rows left-padded by different amounts and by a common prefix,
+    against the untrimmed single-sequence oracle forward of each row.  The
+    common prefix is kept by default, as the reference's CUDA extension
+    does (ext/QwenDecisionCoreCUDAExt.jl:12-20), and trimmed
+    (src/backbone.jl:44-51) with trim_padding=True or
+    QDC_B200_TRIM_PADDING=1."""
     import qdc_b200
     from oracle import forward as F
+    from qdc_b200 import backbone as BB
     from qdc_b200.model import load_weights
     monkeypatch.setenv("QDC_B200_GRAPH", "0")
+    monkeypatch.delenv("QDC_B200_TRIM_PADDING", raising=False)
+    if trim == "env":
+        monkeypatch.setenv("QDC_B200_TRIM_PADDING", "1")
     cfg, w = load_weights(GOLDEN)
     model = cpu_backbone(cfg, w)
+    seen = []
+    real = BB.QwenBackbone.batch_hidden
+    monkeypatch.setattr(BB.QwenBackbone, "batch_hidden",
+                        lambda self, ids, mask=None, last_only=False:
+                        seen.append(np.asarray(ids).shape) or real(self, ids, mask, last_only))
     S = 40
     ids = np.array([(np.arange(S) * (5 + r)) % 64 for r in range(3)])
     mask = np.ones((3, S), np.int64)
     for r, pad in enumerate((4, 9, 6)):
         mask[r, :pad] = 0
     mask[2, 20] = 0  # a hole inside a row as well
-    out = qdc_b200.batch_backbone_hidden(model, ids, mask)
+    kw = {} if trim in (None, "env") else {"trim_padding": trim}
+    out = qdc_b200.batch_backbone_hidden(model, ids, mask, **kw)
     assert out.shape == (3, cfg.hidden)
+    trimmed = trim in (True, "env")
+    assert seen == [(3, S - 4 if trimmed else S)]
     om = F.load_model(GOLDEN)
     for r in range(3):
         expected = F.backbone_hidden(om, ids[r], mask[r])[-1]

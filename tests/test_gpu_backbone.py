@@ -6,7 +6,7 @@ Mirrors the reference's hardware suite (test/cuda.jl:7-31: GPU vs CPU on the
 fixture and a synthetic hybrid backbone, lengths 1..257, masks with holes
 every third token, atol = rtol = 2e-5) and its fixture test
 (test/backbone.jl:1-34).  The site-level test replays every per-layer kernel
-call of a BASELINE config-1 forward through the oracle and checks it at the
+call of a tiny hybrid forward (hidden 256, 4 layers) through the oracle and checks it at the
 kernel bar (1e-6 + 1e-5 |b|)."""
 import json
 import os
@@ -109,7 +109,7 @@ def test_fixture_validation(q, fixture_model):
 
 
 def config1():
-    """vocab 4096, hidden 256, [GDN, GDN, GDN, full], 4 q /
+    """The tiny hybrid backbone: vocab 4096, hidden 256, [GDN, GDN, GDN, full], 4 q /
     2 kv heads x 64, rotary 16 of 64, theta 1e7, eps 1e-6, intermediate 768;
     DeltaNet heads of the reference's synthetic backbone (benchmark/synthetic.jl:4-6:
     key 2 x 128, value 4 x 128)."""
@@ -159,7 +159,7 @@ def test_config1_last_hidden(q, cfg1_pair, n):
 
 
 def test_config1_batch_two_by_64(q, cfg1_pair):
-    """BASELINE config 1's batch: 2 x 64, full mask, both rows in one pass."""
+    """The tiny backbone's batch: 2 x 64, full mask, both rows in one pass."""
     from oracle import forward as F
     model, omodel = cfg1_pair
     rng = np.random.default_rng(0)
@@ -298,26 +298,29 @@ def test_delta_keys_64_wide(q):
                           expected.astype(np.float64)) <= 1.0
 
 
-def test_batch_backbone_hidden_matches_rows(q, fixture_model, monkeypatch):
+@pytest.mark.parametrize("trim", [False, True])
+def test_batch_backbone_hidden_matches_rows(q, fixture_model, monkeypatch, trim):
     """The batched hook on the GPU (one graphed last-token forward for all
     rows) against backbone_last_hidden of each row alone, left padding of
-    different lengths, a common padded prefix trimmed; replays repeat
-    exactly; the eager path agrees within the bar."""
+    different lengths and a common padded prefix -- kept (the default, as
+    the reference's CUDA extension keeps complete sequences) or trimmed;
+    replays repeat exactly; the eager path agrees within the bar."""
     S = 70
     ids = np.array([(np.arange(S) * (3 + r)) % 64 for r in range(4)])
     mask = np.ones((4, S), np.int64)
     for r, pad in enumerate((2, 7, 30, 2)):
         mask[r, :pad] = 0
     mask[3, 0:S - 1:3] = 0
-    got = q.batch_backbone_hidden(fixture_model, ids, mask)
+    got = q.batch_backbone_hidden(fixture_model, ids, mask, trim_padding=trim)
     assert got.shape == (4, fixture_model.config.hidden)
+    assert (4, S - 2 if trim else S, False) in fixture_model._graphs
     for r in range(4):
         alone = q.backbone_last_hidden(fixture_model, ids[r], mask[r]).astype(np.float64)
         assert _violation(got[r].astype(np.float64), alone) <= 1.0
-    again = q.batch_backbone_hidden(fixture_model, ids, mask)
+    again = q.batch_backbone_hidden(fixture_model, ids, mask, trim_padding=trim)
     assert np.array_equal(again, got)
     monkeypatch.setenv("QDC_B200_GRAPH", "0")
-    eager = q.batch_backbone_hidden(fixture_model, ids, mask)
+    eager = q.batch_backbone_hidden(fixture_model, ids, mask, trim_padding=trim)
     assert _violation(eager.astype(np.float64), got.astype(np.float64)) <= 1.0
 
 

@@ -1,4 +1,5 @@
-"""Parity at the BASELINE full sizes (configs 2-5), kernel by kernel, against
+"""Parity at the full benchmark sizes (16,384-65,536 tokens of the 0.8B-shaped
+backbone), kernel by kernel, against
 the oracle run multi-threaded on the host.  Each case also exercises the
 launch shape chosen for large unit counts."""
 import os

@@ -4,7 +4,7 @@ Bar: the gather bit-exact; Float32 outputs within |a - b| <= 1e-6 + 1e-5 |b|;
 bf16-stored outputs within 1e-2 relative.  Cases follow the reference's op
 tests (odd widths 1/7, rows 0/1/17, rotary 0/2/4, packed projection
 layouts, NaN-filled outputs that must be overwritten, inputs unchanged) plus
-the BASELINE shapes (hidden 1024, head_dim 256 / rotary 64, Dv 128,
+the 0.8B-shaped backbone's shapes (hidden 1024, head_dim 256 / rotary 64, Dv 128,
 intermediate 3584).
 """
 import os

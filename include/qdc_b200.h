@@ -162,11 +162,16 @@ QDC_API int qdc_gather_rms_device_ids(qdc_ctx *ctx, void *out_x, void *out_y,
  * and deployments with a memory budget fixed at start-up.  The ids are
  * staged in a fixed 256 KiB array inside the library's device image, so a
  * call takes at most 65536 ids (more: QDC_EINVAL).  Runs on the current
- * device; its first call there looks the array up (cudaGetSymbolAddress),
- * so make it before any stream capture.  All calls on a device share that
- * array: calls whose work overlaps on the GPU race -- serialise them (calls
- * on one stream are ordered).  Ids are validated on the host (QDC_EBOUNDS);
- * errors are reported through qdc_last_error(NULL). */
+ * device.  Its first call there looks the array up (cudaGetSymbolAddress)
+ * and, under CUDA's lazy module loading (the default), is when the driver
+ * loads the library's module onto that device and commits the array: make
+ * that first call at start-up, before any stream capture begins.  The
+ * looked-up address is kept for the process; cudaDeviceReset is not
+ * supported.  All calls on a device share the array: calls whose work
+ * overlaps on the GPU race -- serialise them (calls on one stream are
+ * ordered).  Ids are validated on the host (QDC_EBOUNDS); an out-of-range id
+ * that racing calls let through reaches the device as a NaN row (there is no
+ * device flag).  Errors are reported through qdc_last_error(NULL). */
 QDC_API int qdc_gather_rms_noalloc(void *out_x, void *out_y, const void *table,
                                    const int32_t *ids, const void *add,
                                    const float *gamma, float eps, int centered,

@@ -89,12 +89,15 @@ struct DeviceGuard {
     }
 };
 
+}  // namespace
+
 // Blocks per SM that keep one instance of `kernel` resident, cached per
-// (kernel, device).
-int resident_blocks(const void* kernel, int device, int threads) {
+// (kernel, device, block size).  Shared with qdc_noalloc.cu (not exported).
+int qdc_resident_blocks(const void* kernel, int device, int threads) {
     static std::mutex mu;
     static std::unordered_map<uint64_t, int> cache;
-    const uint64_t key = reinterpret_cast<uint64_t>(kernel) ^ (uint64_t(device) << 56);
+    const uint64_t key = reinterpret_cast<uint64_t>(kernel) ^ (uint64_t(device) << 56) ^
+                         (uint64_t(threads) << 40);
     {
         std::lock_guard<std::mutex> lock(mu);
         auto it = cache.find(key);
@@ -106,6 +109,12 @@ int resident_blocks(const void* kernel, int device, int threads) {
     std::lock_guard<std::mutex> lock(mu);
     cache[key] = n;
     return n;
+}
+
+namespace {
+
+int resident_blocks(const void* kernel, int device, int threads) {
+    return qdc_resident_blocks(kernel, device, threads);
 }
 
 // Persistent grid of at most one full wave, balanced: with R grid-stride
@@ -149,42 +158,6 @@ int launch(qdc_ctx* ctx, void (*kernel)(Args), int grid, const Args& args, void*
 // ---------------------------------------------------------------- row ops
 
 template <typename T>
-using RowKernel = void (*)(qdc::RowArgs);
-
-template <typename T>
-RowKernel<T> row_vec_kernel(int64_t chunks);
-
-template <>
-RowKernel<float> row_vec_kernel<float>(int64_t chunks) {
-    switch (chunks) {
-        case 1: return qdc::row_rms_vec<float, 1, 1>;
-        case 2: return qdc::row_rms_vec<float, 2, 1>;
-        case 3: return qdc::row_rms_vec<float, 3, 1>;
-        case 4: return qdc::row_rms_vec<float, 4, 1>;
-        case 6: return qdc::row_rms_vec<float, 6, 1>;
-        case 8: return qdc::row_rms_vec<float, 8, 1>;
-        case 12: return qdc::row_rms_vec<float, 12, 1>;
-        case 16: return qdc::row_rms_vec<float, 16, 1>;
-        default: return nullptr;
-    }
-}
-
-template <>
-RowKernel<uint16_t> row_vec_kernel<uint16_t>(int64_t chunks) {
-    switch (chunks) {
-        case 1: return qdc::row_rms_vec<uint16_t, 1, 1>;
-        case 2: return qdc::row_rms_vec<uint16_t, 2, 1>;
-        case 3: return qdc::row_rms_vec<uint16_t, 3, 1>;
-        case 4: return qdc::row_rms_vec<uint16_t, 4, 1>;
-        case 6: return qdc::row_rms_vec<uint16_t, 6, 1>;
-        case 8: return qdc::row_rms_vec<uint16_t, 8, 1>;
-        case 12: return qdc::row_rms_vec<uint16_t, 12, 1>;
-        case 16: return qdc::row_rms_vec<uint16_t, 16, 1>;
-        default: return nullptr;
-    }
-}
-
-template <typename T>
 int launch_rows(qdc_ctx* ctx, const qdc::RowArgs& a, void* stream) {
     if (a.rows == 0) return QDC_OK;
     constexpr int64_t N = 16 / sizeof(T);
@@ -195,8 +168,7 @@ int launch_rows(qdc_ctx* ctx, const qdc::RowArgs& a, void* stream) {
                (a.ld_x * e) % 16 == 0 && (a.ld_y * e) % 16 == 0 &&
                (a.out_r == nullptr || (a.ld_r * e) % 16 == 0) &&
                (a.m == nullptr || (a.ld_m * e) % 16 == 0);
-    RowKernel<T> k = vec ? row_vec_kernel<T>(a.width / (32 * N)) : nullptr;
-    if (k == nullptr) k = qdc::row_rms_generic<T>;
+    const qdc::RowKernel k = qdc::row_kernel_for<T>(a.width, vec);
     const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, a.rows);
     return launch(ctx, k, grid, a, stream, "row_rms");
 }

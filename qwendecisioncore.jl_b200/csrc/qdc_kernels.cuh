@@ -227,7 +227,7 @@ struct RowArgs {
     const void* m;
     const float* gamma;
     const int32_t* ids;  // device ids: x row = x + ids[row] * ld_x
-    int* flag;           // raised on an out-of-range id
+    int* flag;           // raised on an out-of-range id (NULL: the NaN row only)
     float eps;
     int centered;
     int64_t rows, width, ld_x, ld_m, ld_r, ld_y, vocab;
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
             s = segment_sum<32>(s);
             const float scale = rms_scale(s, 1.0f / float(W), a.eps);
             if (bad[k]) {
-                if (lane == 0) atomicOr(a.flag, 1);
+                if (lane == 0 && a.flag) atomicOr(a.flag, 1);
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c)
 #pragma unroll
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
         }
         s = segment_sum<32>(s);
         const float scale = rms_scale(s, inv_width, a.eps);
-        if (bad && lane == 0) atomicOr(a.flag, 1);
+        if (bad && lane == 0 && a.flag) atomicOr(a.flag, 1);
         T* rr = a.out_r ? static_cast<T*>(a.out_r) + row * a.ld_r : nullptr;
         T* yr = a.out_y ? static_cast<T*>(a.out_y) + row * a.ld_y : nullptr;
         for (int64_t i = lane; i < a.width; i += 32) {
@@ -365,6 +365,31 @@ __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
             }
         }
     }
+}
+
+// The row kernel for `width` columns of T: the vector kernel specialised on
+// the 16-byte chunks per lane when every operand allows it (`vec`), the
+// scalar two-pass kernel otherwise.  Host code; shared by every entry point
+// that launches the row kernels.
+using RowKernel = void (*)(RowArgs);
+
+template <typename T>
+inline RowKernel row_kernel_for(int64_t width, bool vec) {
+    constexpr int64_t N = 16 / sizeof(T);
+    if (vec && width % (32 * N) == 0) {
+        switch (width / (32 * N)) {
+            case 1: return row_rms_vec<T, 1, 1>;
+            case 2: return row_rms_vec<T, 2, 1>;
+            case 3: return row_rms_vec<T, 3, 1>;
+            case 4: return row_rms_vec<T, 4, 1>;
+            case 6: return row_rms_vec<T, 6, 1>;
+            case 8: return row_rms_vec<T, 8, 1>;
+            case 12: return row_rms_vec<T, 12, 1>;
+            case 16: return row_rms_vec<T, 16, 1>;
+            default: break;
+        }
+    }
+    return row_rms_generic<T>;
 }
 
 // ----------------------------------------------------------- head kernels

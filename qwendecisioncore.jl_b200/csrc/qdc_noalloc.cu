@@ -12,20 +12,26 @@
 // calls no allocator: its scratch lives in a fixed array in this library's
 // device image.
 //
-// The scratch.  `g_noalloc_scratch` is a file-scope __device__ array of
-// QDC_NOALLOC_MAX_IDS staged ids plus one 256-byte slot for the device error
-// flag: 256 KiB + 256 B, held on every GPU that loads the library until the
-// process exits.  Its host-side name is only a stand-in for the symbol, so
-// the device address is looked up once per device with cudaGetSymbolAddress
-// while that device is current.  That set-up happens inside the first call on
-// each device; make that first call before capturing a CUDA graph.
+// The scratch.  `g_noalloc_ids` is a file-scope __device__ array of
+// QDC_NOALLOC_MAX_IDS staged ids (256 KiB), held on every GPU that loads the
+// library until the process exits.  Its host-side name is only a stand-in
+// for the symbol, so the device address is looked up once per device with
+// cudaGetSymbolAddress while that device is current.  That set-up happens
+// inside the first call on each device, and under CUDA's lazy module loading
+// (the default) that first call is also when the driver loads this file's
+// module onto the device and commits the array: make the first call at
+// start-up, and before any stream capture begins.  The cached address
+// belongs to the device's primary context; cudaDeviceReset is not supported
+// (after a reset the cached address is stale).
 //
 // Sharing.  Every call on a device uses the same array and it keeps the last
-// call's contents: each call re-stages its ids and clears the flag before its
-// kernel.  Calls on one stream are ordered; calls whose work overlaps on the
-// GPU (different streams, or host threads racing on one device) overwrite
-// each other's ids -- serialise them.  Errors are reported through the
-// status code and qdc_last_error(NULL).
+// call's contents: each call re-stages its ids before its kernel.  Calls on
+// one stream are ordered; calls whose work overlaps on the GPU (different
+// streams, or host threads racing on one device) overwrite each other's ids
+// -- serialise them.  Ids are validated on the host, so a serialised call
+// never meets an out-of-range id on the device; if racing calls let one
+// through, its row is filled with NaN (there is no device flag to read).
+// Errors are reported through the status code and qdc_last_error(NULL).
 #include "qdc_b200.h"
 #include "qdc_kernels.cuh"
 
@@ -37,15 +43,12 @@
 #define QDC_NOALLOC_MAX_IDS (64 * 1024)
 #define QDC_NOALLOC_MAX_DEVICES 64
 
-namespace {
+static __device__ __align__(256) int32_t g_noalloc_ids[QDC_NOALLOC_MAX_IDS];
 
-// [0, QDC_NOALLOC_MAX_IDS): staged ids; then 64 ints (256 B) holding the flag.
-__device__ __align__(256) int32_t g_noalloc_scratch[QDC_NOALLOC_MAX_IDS + 64];
-
-}  // namespace
-
-// Defined in qdc_b200.cu: the per-thread text qdc_last_error(NULL) returns.
+// Defined in qdc_b200.cu (not exported): the per-thread text that
+// qdc_last_error(NULL) returns, and the cached occupancy query.
 void qdc_set_thread_error(const char* msg);
+int qdc_resident_blocks(const void* kernel, int device, int threads);
 
 namespace {
 
@@ -58,48 +61,31 @@ int noalloc_fail(int status, const char* msg, const char* detail = nullptr) {
 
 struct DeviceScratch {
     int32_t* ids = nullptr;
-    int* flag = nullptr;
     int sm_count = 0;
 };
 
 std::mutex g_setup_mu;
 DeviceScratch g_scratch[QDC_NOALLOC_MAX_DEVICES];
 
-// Device address of the scratch array and the SM count of `device`, looked
-// up once per device (the device must be current).
+// Device address of the id array and the SM count of `device`, looked up
+// once per device (the device must be current).
 int setup(int device, DeviceScratch* out) {
     std::lock_guard<std::mutex> lock(g_setup_mu);
     DeviceScratch& s = g_scratch[device];
     if (s.ids == nullptr) {
-        void* base = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&base, g_noalloc_scratch);
-        if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "cudaGetSymbolAddress", cudaGetErrorString(e));
         int major = 0, sms = 0;
-        e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+        cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "cudaDeviceGetAttribute", cudaGetErrorString(e));
         if (major != 10) return noalloc_fail(QDC_EDEVICE, "libqdc_b200 is built for sm_100a");
+        void* base = nullptr;
+        e = cudaGetSymbolAddress(&base, g_noalloc_ids);
+        if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "cudaGetSymbolAddress", cudaGetErrorString(e));
         s.ids = static_cast<int32_t*>(base);
-        s.flag = reinterpret_cast<int*>(static_cast<int32_t*>(base) + QDC_NOALLOC_MAX_IDS);
         s.sm_count = sms;
     }
     *out = s;
     return QDC_OK;
-}
-
-template <typename T>
-void (*pick_kernel(int64_t width, bool vec))(qdc::RowArgs) {
-    constexpr int64_t N = 16 / sizeof(T);
-    if (vec && width % (32 * N) == 0) {
-        switch (width / (32 * N)) {
-            case 1: return qdc::row_rms_vec<T, 1, 1>;
-            case 2: return qdc::row_rms_vec<T, 2, 1>;
-            case 4: return qdc::row_rms_vec<T, 4, 1>;
-            case 8: return qdc::row_rms_vec<T, 8, 1>;
-            default: break;
-        }
-    }
-    return qdc::row_rms_generic<T>;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -129,29 +115,28 @@ extern "C" int qdc_gather_rms_noalloc(void* out_x, void* out_y, const void* tabl
     DeviceScratch s;
     if (int st = setup(device, &s)) return st;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    e = cudaMemsetAsync(s.flag, 0, sizeof(int), st);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(s.ids, ids, size_t(n) * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+    e = cudaMemcpyAsync(s.ids, ids, size_t(n) * sizeof(int32_t), cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "staging ids", cudaGetErrorString(e));
 
-    qdc::RowArgs a{out_x, out_y, table, add, gamma, s.ids, s.flag, eps, centered ? 1 : 0,
+    qdc::RowArgs a{out_x, out_y, table, add, gamma, s.ids, nullptr, eps, centered ? 1 : 0,
                    n, hidden, hidden, hidden, hidden, hidden, vocab};
     const int64_t esz = dtype == QDC_F32 ? 4 : 2;
     const bool vec = aligned16(table) && aligned16(out_x) && aligned16(out_y) && aligned16(add) &&
                      aligned16(gamma) && (hidden * esz) % 16 == 0;
-    void (*k)(qdc::RowArgs) = dtype == QDC_F32 ? pick_kernel<float>(hidden, vec)
-                                               : pick_kernel<uint16_t>(hidden, vec);
-    int per_sm = 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, qdc::kThreads, 0) != cudaSuccess ||
-        per_sm < 1)
-        per_sm = 1;
+    const qdc::RowKernel k = dtype == QDC_F32 ? qdc::row_kernel_for<float>(hidden, vec)
+                                              : qdc::row_kernel_for<uint16_t>(hidden, vec);
+    // persistent grid of at most one wave, every grid-stride round full
     const int64_t warps = qdc::kThreads / 32;
-    const int64_t cap = int64_t(s.sm_count) * per_sm;
+    const int64_t cap = int64_t(s.sm_count) *
+                        qdc_resident_blocks(reinterpret_cast<const void*>(k), device, qdc::kThreads);
     const int64_t rounds = (n + cap * warps - 1) / (cap * warps);
     int64_t grid = (n + rounds * warps - 1) / (rounds * warps);
     if (grid > cap) grid = cap;
-    k<<<unsigned(grid < 1 ? 1 : grid), qdc::kThreads, 0, st>>>(a);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid < 1 ? 1 : grid));
+    cfg.blockDim = dim3(unsigned(qdc::kThreads));
+    cfg.stream = st;
+    e = cudaLaunchKernelEx(&cfg, k, a);
     if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "launch", cudaGetErrorString(e));
     return QDC_OK;
 }

@@ -47,6 +47,7 @@ const CONTEXT_LOCK = ReentrantLock()
 function check(status::Cint, handle::Ptr{Cvoid} = C_NULL)
     status == QDC_OK && return nothing
     msg = unsafe_string(ccall((:qdc_last_error, LIB), Cstring, (Ptr{Cvoid},), handle))
+    isempty(msg) && (msg = unsafe_string(ccall((:qdc_status_string, LIB), Cstring, (Cint,), status)))
     # src/backbone.jl:413-422 raises ArgumentError for bad ids and shapes
     status in (QDC_EINVAL, QDC_EBOUNDS) && throw(ArgumentError(msg))
     error("libqdc_b200: " * msg)
@@ -65,7 +66,10 @@ function context(dev::CUDA.CuDevice = CUDA.device())
     end
 end
 
-use_b200() = CUDA.functional() && CUDA.capability(CUDA.device()) == v"10.0" && isfile(LIB)
+const QDC_B200_ABI_VERSION = Cint(1)
+
+use_b200() = CUDA.functional() && CUDA.capability(CUDA.device()) == v"10.0" && isfile(LIB) &&
+             ccall((:qdc_abi_version, LIB), Cint, ()) == QDC_B200_ABI_VERSION
 
 stream_handle() = Base.unsafe_convert(Ptr{Cvoid}, CUDA.stream().handle)
 ptr(x::CUDA.CuArray) = Base.unsafe_convert(Ptr{Cvoid}, pointer(x))
@@ -280,6 +284,24 @@ function gather_rms_device!(out_x, out_y, embedding::CUDA.CuMatrix{Float32}, ids
     return out_x, out_y
 end
 
+"""gather_rms_noalloc!(out_x, out_y, embedding, ids, weight, eps)  -- gather_rms!
+for a host whose memory pool owns every device byte: the library allocates
+nothing (no context; ids staged in a fixed 256 KiB array in the library, at
+most 65536 per call).  Make the first call on a device at start-up; calls
+whose work overlaps on the GPU race on the array, so keep them on one
+stream."""
+function gather_rms_noalloc!(out_x, out_y, embedding::CUDA.CuMatrix{Float32}, ids::Vector{<:Integer},
+                             weight, eps)
+    hidden, vocab = size(embedding)
+    host = Int32.(ids)
+    check(ccall((:qdc_gather_rms_noalloc, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Int32}, Ptr{Cvoid}, Ptr{Cvoid}, Cfloat, Cint,
+                 Int64, Int64, Int64, Cint, Ptr{Cvoid}),
+                ptr(out_x), ptr(out_y), ptr(embedding), host, C_NULL, ptr(weight), Float32(eps), Cint(1),
+                Int64(length(host)), Int64(hidden), Int64(vocab), QDC_F32, stream_handle()))
+    return out_x, out_y
+end
+
 """q_k_norm_rope!(q, k, projected, q_norm, k_norm, eps, rotary, cos, sin; q_width, k_offset)
 
 The query heads (first dim of each 2dim-wide [q; gate] head) and the key
@@ -327,6 +349,26 @@ ws_reserve!(bytes::Integer) = check(ccall((:qdc_ws_reserve, LIB), Cint, (Ptr{Cvo
                                           context().handle, Csize_t(bytes)), context().handle)
 ws_reset!() = check(ccall((:qdc_ws_reset, LIB), Cint, (Ptr{Cvoid},), context().handle), context().handle)
 
+"""ws_mark() / ws_release!(mark) -- the cursor before a layer, and back to it
+after: each layer of a kind then carves the same slots in the same order,
+as the per-kind slot lists of ext/cuda_workspace.jl:279-300 do."""
+function ws_mark()
+    ref = Ref{Csize_t}(0)
+    check(ccall((:qdc_ws_mark, LIB), Cint, (Ptr{Cvoid}, Ptr{Csize_t}), context().handle, ref),
+          context().handle)
+    return ref[]
+end
+ws_release!(mark::Integer) = check(ccall((:qdc_ws_release, LIB), Cint, (Ptr{Cvoid}, Csize_t),
+                                         context().handle, Csize_t(mark)), context().handle)
+
+"""ws_stats() -> (used, capacity, high_water) bytes of the arena."""
+function ws_stats()
+    used, cap, high = Ref{Csize_t}(0), Ref{Csize_t}(0), Ref{Csize_t}(0)
+    check(ccall((:qdc_ws_stats, LIB), Cint, (Ptr{Cvoid}, Ptr{Csize_t}, Ptr{Csize_t}, Ptr{Csize_t}),
+                context().handle, used, cap, high), context().handle)
+    return Int(used[]), Int(cap[]), Int(high[])
+end
+
 """scratch(T, dims...) -> CuArray{T} carved from the context's arena (not owned:
 valid until the next ws_reset!())."""
 function scratch(::Type{T}, dims::Integer...) where {T}
@@ -349,11 +391,13 @@ function __init__()
     if use_b200()
         cuda_ext = Base.get_extension(QDC, :QwenDecisionCoreCUDAExt)
         cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!, gather!,
-                                                          gather_rms_device!, qk_norm_rope!,
+                                                          gather_rms_device!, gather_rms_noalloc!,
+                                                          qk_norm_rope!,
                                                           q_k_norm_rope!, rope_tables, gated_rms!,
                                                           swiglu!, attn_gate!, delta_gates!,
                                                           delta_conv_norm!, upload_bf16, to_bf16!,
                                                           set_pdl!, ws_reserve!, ws_reset!,
+                                                          ws_mark, ws_release!, ws_stats,
                                                           scratch, sync!))
     end
 end

@@ -170,81 +170,155 @@ def test_config1_batch_two_by_64(q, cfg1_pair):
         assert _violation(out[b].astype(np.float64), expected.astype(np.float64)) <= 1.0
 
 
-def test_config1_every_kernel_site(q, cfg1_pair, oracle):
-    """Every per-layer kernel call of a config-1 forward, replayed through
-    the oracle on the same inputs, within 1e-6 + 1e-5 |b|."""
-    model, omodel = cfg1_pair
+def check_every_site(model, trace, ids, S, oracle):
+    """Replays every per-layer kernel call recorded in `trace` (a forward of
+    B sequences of S tokens, ids flat (B*S,)) through the oracle on the same
+    inputs, with the model's own weights, at the kernel bar
+    1e-6 + 1e-5 |b| (the gather and the residuals bit-exact).  Returns the
+    number of sites checked."""
     cfg = model.config
-    rng = np.random.default_rng(1)
-    ids = rng.integers(0, 4096, (2, 64))
-    model.trace = []
-    try:
-        model.batch_hidden(ids)
-        trace = model.trace
-    finally:
-        model.trace = None
     n_layers = len(cfg.layer_types)
     kinds = [site for site, _, _ in trace]
+    n_delta = sum(1 for k in cfg.layer_types if k == "linear_attention")
+    n_full = n_layers - n_delta
     assert kinds.count("gather_rms") == 1 and kinds.count("post_rms") == n_layers
-    assert kinds.count("swiglu") == n_layers and kinds.count("gated_rms") == 3
-    assert kinds.count("q_norm_rope") == 1 and kinds.count("k_norm_rope") == 1
+    assert kinds.count("swiglu") == n_layers and kinds.count("gated_rms") == n_delta
+    assert kinds.count("q_norm_rope") == n_full and kinds.count("k_norm_rope") == n_full
     assert kinds.count("mlp_rms") == n_layers - 1 and kinds.count("final_rms") == 1
-    assert kinds.count("delta_conv_norm") == 3 and kinds.count("attn_gate") == 1
-    assert kinds.count("delta_gates") == 3
-    w = omodel.weights
-    cos, sin = oracle.rope_table(cfg.rope_theta, cfg.rotary_dim, 64)
-    layer = 0
-
-    def cpu(t):
-        return t.cpu().numpy()
+    assert kinds.count("delta_conv_norm") == n_delta and kinds.count("attn_gate") == n_full
+    assert kinds.count("delta_gates") == n_delta
+    cos, sin = oracle.rope_table(cfg.rope_theta, cfg.rotary_dim, S)
+    cpu = lambda t: t.detach().cpu().numpy()
+    layers = model.layers
 
     def close(a, e):
         a, e = np.asarray(a, np.float64), np.asarray(e, np.float64)
         return bool((np.abs(a - e) <= 1e-6 + 1e-5 * np.abs(e)).all())
 
+    layer = 0
     for site, ins, outs in trace:
-        p = f"layers.{layer}."
+        lay = layers[min(layer, n_layers - 1)]
         if site == "gather_rms":
-            ex_x, ex_y = oracle.gather_rms(w["embed_tokens.weight"], ids.reshape(-1), None,
-                                           w["layers.0.input_layernorm.weight"], cfg.eps)
+            ex_x, ex_y = oracle.gather_rms(cpu(model.embedding), np.asarray(ids, np.int32), None,
+                                           cpu(layers[0]["input_norm"]), cfg.eps)
             assert np.array_equal(cpu(outs[0]), ex_x) and close(cpu(outs[1]), ex_y)
         elif site in ("q_norm_rope", "k_norm_rope"):
-            x = cpu(ins[0])
-            gam = w[p + ("self_attn.q_norm.weight" if site[0] == "q" else "self_attn.k_norm.weight")]
-            ex = oracle.qk_norm_rope(np.ascontiguousarray(x), gam, cfg.eps, cfg.rotary_dim, cos, sin,
-                                     seq_len=64)
-            assert close(cpu(outs[0]), ex), site
+            gam = cpu(lay["q_norm"] if site[0] == "q" else lay["k_norm"])
+            ex = oracle.qk_norm_rope(np.ascontiguousarray(cpu(ins[0])), gam, cfg.eps, cfg.rotary_dim,
+                                     cos, sin, seq_len=S)
+            assert close(cpu(outs[0]), ex), (site, layer)
         elif site == "delta_conv_norm":
             C = 2 * cfg.key_heads * cfg.key_dim + cfg.value_heads * cfg.value_dim
             eq, ek, ev = oracle.delta_conv_norm(np.ascontiguousarray(cpu(ins[0])),
                                                 cpu(ins[1]).reshape(C, 4), cfg.key_heads, cfg.key_dim,
-                                                cfg.value_heads, cfg.value_dim, seq_len=64)
-            assert close(cpu(outs[0]), eq) and close(cpu(outs[1]), ek) and close(cpu(outs[2]), ev)
+                                                cfg.value_heads, cfg.value_dim, seq_len=S)
+            assert close(cpu(outs[0]), eq) and close(cpu(outs[1]), ek) and close(cpu(outs[2]), ev), \
+                (site, layer)
         elif site == "delta_gates":
-            H = cfg.value_heads
-            lay = model.layers[layer]
-            eb, ed = oracle.delta_gates(np.ascontiguousarray(cpu(ins[0])), 0, H, cpu(lay["a_decay"]),
-                                        cpu(lay["dt_bias"]))
-            assert close(cpu(outs[0]), eb) and close(cpu(outs[1]), ed), site
+            eb, ed = oracle.delta_gates(np.ascontiguousarray(cpu(ins[0])), 0, cfg.value_heads,
+                                        cpu(lay["a_decay"]), cpu(lay["dt_bias"]))
+            assert close(cpu(outs[0]), eb) and close(cpu(outs[1]), ed), (site, layer)
         elif site == "attn_gate":
             ex = oracle.attn_gate(np.ascontiguousarray(cpu(ins[0])), np.ascontiguousarray(cpu(ins[1])))
-            assert close(cpu(outs[0]), ex), site
+            assert close(cpu(outs[0]), ex), (site, layer)
         elif site == "gated_rms":
-            o, z = cpu(ins[0]), np.ascontiguousarray(cpu(ins[1]))
-            ex = oracle.gated_rms(o, z, w[p + "linear_attn.norm.weight"], cfg.eps)
-            assert close(cpu(outs[0]), ex), site
+            ex = oracle.gated_rms(cpu(ins[0]), np.ascontiguousarray(cpu(ins[1])), cpu(lay["norm"]), cfg.eps)
+            assert close(cpu(outs[0]), ex), (site, layer)
         elif site == "post_rms":
-            ex_r, ex_y = oracle.residual_rms(cpu(ins[0]), cpu(ins[1]),
-                                             w[p + "post_attention_layernorm.weight"], cfg.eps)
-            assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), site
+            ex_r, ex_y = oracle.residual_rms(cpu(ins[0]), cpu(ins[1]), cpu(lay["post_norm"]), cfg.eps)
+            assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), (site, layer)
         elif site == "swiglu":
             ex, _ = oracle.swiglu(np.ascontiguousarray(cpu(ins[0])), np.ascontiguousarray(cpu(ins[1])))
-            assert close(cpu(outs[0]), ex), site
+            assert close(cpu(outs[0]), ex), (site, layer)
         elif site in ("mlp_rms", "final_rms"):
-            gam = w[f"layers.{layer + 1}.input_layernorm.weight"] if site == "mlp_rms" else w["norm.weight"]
+            gam = cpu(layers[layer + 1]["input_norm"] if site == "mlp_rms" else model.final_norm)
             ex_r, ex_y = oracle.residual_rms(cpu(ins[0]), cpu(ins[1]), gam, cfg.eps)
-            assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), site
+            assert np.array_equal(cpu(outs[0]), ex_r) and close(cpu(outs[1]), ex_y), (site, layer)
             layer += 1
+        else:
+            raise AssertionError(f"unexpected site {site}")
+    assert layer == n_layers
+    return len(trace)
+
+
+def traced_forward(model, ids, mask=None):
+    """batch_hidden of (B, S) ids with every per-layer kernel call recorded."""
+    model.trace = []
+    try:
+        out = model.batch_hidden(ids, mask)
+        return out, model.trace
+    finally:
+        model.trace = None
+
+
+def test_config1_every_kernel_site(q, cfg1_pair, oracle):
+    """Every per-layer kernel call of a tiny-hybrid forward (2 x 64),
+    replayed through the oracle on the same inputs, within 1e-6 + 1e-5 |b|."""
+    model, _ = cfg1_pair
+    ids = np.random.default_rng(1).integers(0, 4096, (2, 64))
+    _, trace = traced_forward(model, ids)
+    assert check_every_site(model, trace, ids.reshape(-1), 64, oracle) == len(trace)
+
+
+def config_0p8b():
+    """The 0.8B-shaped hybrid backbone the benchmark times: 24 layers
+    [GDN, GDN, GDN, full] x 6, hidden 1024, intermediate 3584, DeltaNet keys
+    and values 16 x 128, attention 8 q / 2 kv heads x 256 with partial RoPE
+    on 64 dims, theta 1e7, vocab 151936."""
+    from qdc_b200.model import Config
+    return Config(hidden=1024, head_dim=256, heads=8, kv_heads=2, key_heads=16, value_heads=16,
+                  key_dim=128, value_dim=128, eps=float(np.float32(1e-6)),
+                  rope_theta=float(np.float32(1e7)), rotary_dim=64, vocab=151936, intermediate=3584,
+                  layer_types=(["linear_attention"] * 3 + ["full_attention"]) * 6)
+
+
+@pytest.fixture(scope="module")
+def model_0p8b(q, oracle):
+    oracle.set_threads(os.cpu_count() or 1)
+    model = q.QwenBackbone.random(config_0p8b(), seed=5, device="cuda")
+    yield model
+    oracle.set_threads(1)
+    del model
+    torch.cuda.empty_cache()
+
+
+def test_0p8b_every_kernel_site_2048_tokens(model_0p8b, oracle):
+    """The 24-layer 0.8B-shaped forward on one 2048-token sequence: every
+    kernel call (gather + norm, 18 x conv + q/k L2 norms over 48 heads of
+    the packed projection, 18 x DeltaNet gates, 18 x gated norm, 6 x q+k
+    norm + RoPE, 6 x attention gate, 24 x post norm, 24 x SwiGLU, 23 x
+    MLP residual + next norm, the final norm) against the oracle."""
+    ids = np.random.default_rng(2048).integers(0, 151936, (1, 2048))
+    _, trace = traced_forward(model_0p8b, ids)
+    assert check_every_site(model_0p8b, trace, ids.reshape(-1), 2048, oracle) == 1 + 18 * 4 + 6 * 3 + 24 * 3
+
+
+def test_0p8b_short_sequence_with_holes(model_0p8b, oracle):
+    """A short sequence with mask holes every third token (test/cuda.jl:13)
+    and a batch of two: every site against the oracle, and the whole forward
+    against the oracle forward (float64 projections, attention and delta
+    rule) at the whole-forward bar 2e-5."""
+    from oracle import forward as F
+    from qdc_b200.model import random_weights
+    n = 67
+    rng = np.random.default_rng(n)
+    ids = rng.integers(0, 151936, (2, n))
+    mask = np.ones((2, n), np.int64)
+    mask[0, 0:n - 1:3] = 0
+    _, trace = traced_forward(model_0p8b, ids, mask)
+    check_every_site(model_0p8b, trace, ids.reshape(-1), n, oracle)
+    cfg = model_0p8b.config
+    weights = {k: v.cpu().numpy() for k, v in random_weights(cfg, 5, device="cuda").items()}
+    omodel = F.Model(F.Config(**{k: getattr(cfg, k) for k in F.Config.__dataclass_fields__}), weights)
+    expected = F.backbone_hidden(omodel, ids[0], mask[0])
+    del weights, omodel
+    actual = q_hidden(model_0p8b, ids[0], mask[0])
+    assert _violation(actual.astype(np.float64), expected.astype(np.float64)) <= 1.0
+
+
+def q_hidden(model, ids, mask):
+    import qdc_b200
+    return qdc_b200.backbone_hidden(model, ids, mask)
 
 
 def test_last_hidden_shared_across_threads(q, fixture_model):

@@ -95,3 +95,46 @@ def test_config5_gated_rms(q, oracle):
     dp = dev(proj)
     got = q.native_gated_rms(dev(o), dp[:, 6144:8192].view(T, 16, 128), dev(w), 1e-6)
     assert close(got, expected)
+
+
+def test_0p8b_delta_conv_norm_48_heads(q, oracle):
+    """The DeltaNet prologue at the 0.8B backbone's shape: 6,144 channels
+    (16 q + 16 k + 16 v heads of 128) read in place from the packed
+    [qkv | z | a | b] rows (8,224 wide), 32,768 tokens as 16 sequences of
+    2,048 -- the shared-memory pipeline kernel."""
+    rng = np.random.default_rng(6)
+    T, C, W = 32768, 6144, 8224
+    proj = rng.standard_normal((T, W), dtype=np.float32)
+    conv = (rng.standard_normal((C, 4), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
+    eq, ek, ev = oracle.delta_conv_norm(proj, conv, 16, 128, 16, 128, seq_len=2048)
+    gq, gk, gv = q.native_delta_conv_norm(dev(proj), dev(conv), 16, 128, 16, 128, seq_len=2048)
+    assert close(gq, eq) and close(gk, ek) and close(gv, ev)
+
+
+def test_0p8b_attn_gate_8_heads_256(q, oracle):
+    """The attention output gate at the 0.8B backbone's shape: values
+    (16 sequences, 8 heads, 2048, 256) and the gate half of the packed
+    [q;gate] projection (32,768 tokens x 8 x 512)."""
+    rng = np.random.default_rng(7)
+    B, H, S, D = 16, 8, 2048, 256
+    values = rng.standard_normal((B, H, S, D), dtype=np.float32)
+    qgate = rng.standard_normal((B * S, H, 2 * D), dtype=np.float32)
+    expected = oracle.attn_gate(values, np.ascontiguousarray(qgate[:, :, D:]))
+    got = q.native_attn_gate(dev(values), dev(qgate)[:, :, D:])
+    assert close(got, expected)
+
+
+def test_0p8b_delta_gates_16_heads(q, oracle):
+    """The DeltaNet beta / decay gates at the 0.8B backbone's shape: a and b
+    (16 heads each) read from the tail of the packed 8,224-wide projection
+    rows, 65,536 tokens; inputs spread over [-30, 30] so the softplus and
+    sigmoid reach both tails."""
+    rng = np.random.default_rng(8)
+    T, W, start = 65536, 8224, 6144 + 2048
+    proj = rng.standard_normal((T, W), dtype=np.float32)
+    proj[:, start:] = rng.uniform(-30, 30, (T, W - start)).astype(np.float32)
+    a_decay = (-np.exp(rng.uniform(-1, 0.5, 16))).astype(np.float32)
+    dt_bias = rng.standard_normal(16, dtype=np.float32)
+    eb, ed = oracle.delta_gates(proj, start, 16, a_decay, dt_bias)
+    gb, gd = q.native_delta_gates(dev(proj), start, 16, dev(a_decay), dev(dt_bias))
+    assert close(gb, eb) and close(gd, ed)

@@ -81,3 +81,10 @@ def test_ccall_matches_header(name, ret, types, args):
     assert ret == c_ret
     assert [_jl_kind(t) for t in types] == c_kinds
     assert len(args) == len(types), f"{name}: {len(args)} arguments for {len(types)} types"
+
+
+def test_every_declared_entry_point_is_bound():
+    """Every QDC_API function of the header has a ccall in the binding."""
+    bound = {c[0] for c in CALLS}
+    missing = sorted(set(_header()) - bound)
+    assert not missing, f"declared in include/qdc_b200.h but not bound in the Julia extension: {missing}"

@@ -295,6 +295,19 @@ QDC_API int qdc_bf16_to_f32(qdc_ctx *ctx, float *out, const uint16_t *in, int64_
 QDC_API int qdc_f32_to_bf16(qdc_ctx *ctx, uint16_t *out, const float *in, int64_t n,
                             void *stream);
 
+/* In-place batched solve with unit lower-triangular matrices:
+ *   X_b <- (I + strict_lower(L_b))^{-1} X_b,   b = 0 .. batch-1,
+ * L_b an n x n matrix (1 <= n <= 64) at l + b*l_batch with row stride ld_l
+ * (its diagonal and upper triangle are not read), X_b an n x width matrix
+ * at x + b*x_batch with row stride ld_x; the L's and X's must not overlap.
+ * Forward substitution in Float32 (fused multiply-adds, k ascending).
+ * Replaces delta_solve, the chunked gated delta rule's
+ * UnitLowerTriangular(system) \ rhs (src/backbone.jl:279,328-330;
+ * CUDA ext/QwenDecisionCoreCUDAExt.jl:22-24), with no solver workspace. */
+QDC_API int qdc_unit_lower_solve(qdc_ctx *ctx, float *x, const float *l, int64_t batch,
+                                 int n, int64_t width, int64_t ld_l, int64_t l_batch,
+                                 int64_t ld_x, int64_t x_batch, void *stream);
+
 /* SwiGLU gate:  h = silu(g) * u  (src/backbone.jl:196-197,352-355).
  * g/u rows at g + t*ld_g, u + t*ld_u (the packed [gate;up] projection of
  * ext/cuda_mlp.jl:63-71 is g = P, u = P + width, ld = 2*width).  Writes

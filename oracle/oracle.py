@@ -53,6 +53,7 @@ _SIGNATURES = {
     "qdo_attn_gate": (None, [_f32p, _f32p, _f32p, _i64, _i64, _int, _int, _i64, _i64, _i64, _i64,
                              _i64, _i64]),
     "qdo_delta_gates": (None, [_f32p, _f32p, _f32p, _i64, _i64, _f32p, _f32p, _i64, _int]),
+    "qdo_unit_lower_solve": (None, [_f32p, _f32p, _i64, _int, _i64, _i64, _i64, _i64, _i64]),
     "qdo_delta_conv_norm": (None, [_f32p, _f32p, _f32p, _f32p, _i64, _f32p, _i64, _i64, _int,
                                    _int, _int, _int, _flt]),
 }
@@ -318,6 +319,19 @@ def delta_gates(proj, start, heads, a_decay, dt_bias):
         lib().qdo_delta_gates(_p(beta), _p(decay), proj.ctypes.data_as(_f32p), proj.strides[0] // 4,
                               start, _p(a_decay), _p(dt_bias), tokens, heads)
     return beta, decay
+
+
+def unit_lower_solve(system, rhs):
+    """delta_solve (src/backbone.jl:279): UnitLowerTriangular(system) \\ rhs for
+    a batch: system (batch, n, n), rhs (batch, n, width).  Returns the
+    solution (batch, n, width) float32."""
+    L = _f32(system)
+    x = np.array(rhs, dtype=np.float32, order="C", copy=True)
+    batch, n, width = x.shape
+    assert L.shape == (batch, n, n)
+    if x.size:
+        lib().qdo_unit_lower_solve(_p(x), _p(L), batch, n, width, n, n * n, width, n * width)
+    return x
 
 
 def silu(x):

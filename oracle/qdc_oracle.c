@@ -398,3 +398,21 @@ void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,
         }
     }
 }
+
+/* ---- delta_solve, src/backbone.jl:279 ----------------------------------- */
+
+void qdo_unit_lower_solve(float *x, const float *l, int64_t batch, int n,
+                          int64_t width, int64_t ld_l, int64_t l_batch,
+                          int64_t ld_x, int64_t x_batch) {
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
+    for (int64_t b = 0; b < batch; ++b) {
+        const float *lb = l + b * l_batch;
+        float *xb = x + b * x_batch;
+        for (int64_t j = 0; j < width; ++j)
+            for (int i = 1; i < n; ++i) {
+                float acc = xb[i * ld_x + j];
+                for (int k = 0; k < i; ++k) acc = acc - lb[i * ld_l + k] * xb[k * ld_x + j];
+                xb[i * ld_x + j] = acc;
+            }
+    }
+}

@@ -151,6 +151,13 @@ void qdo_delta_gates(float *beta, float *decay, const float *proj, int64_t ld,
 
 /* SwiGLU, src/backbone.jl:352-355: h = silu(g) * u; optional fp32 and/or
  * bf16 (src/safetensors.jl:38-42) outputs. */
+/* delta_solve, src/backbone.jl:279: X_b <- UnitLowerTriangular(L_b) \ X_b
+ * (forward substitution, k ascending, separately rounded Float32 multiply
+ * and subtract; only the strict lower triangle of L_b is read). */
+void qdo_unit_lower_solve(float *x, const float *l, int64_t batch, int n,
+                          int64_t width, int64_t ld_l, int64_t l_batch,
+                          int64_t ld_x, int64_t x_batch);
+
 void qdo_swiglu(float *out_f32, uint16_t *out_bf16, const float *g,
                 const float *u, int64_t rows, int64_t width, int64_t ld_g,
                 int64_t ld_u, int64_t ld_out);

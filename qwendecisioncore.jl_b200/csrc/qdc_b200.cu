@@ -785,6 +785,38 @@ int qdc_f32_to_bf16(qdc_ctx* ctx, uint16_t* out, const float* in, int64_t n, voi
     return convert(ctx, out, in, n, false, stream);
 }
 
+// ------------------------------------------- unit lower-triangular solve
+
+int qdc_unit_lower_solve(qdc_ctx* ctx, float* x, const float* l, int64_t batch, int n, int64_t width,
+                         int64_t ld_l, int64_t l_batch, int64_t ld_x, int64_t x_batch, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (batch < 0 || n < 1 || n > qdc::kTriMax || width < 1)
+        return fail(ctx, QDC_EINVAL, "bad sizes batch=%lld n=%d (1..%d) width=%lld", (long long)batch, n,
+                    qdc::kTriMax, (long long)width);
+    if (batch == 0) return QDC_OK;
+    if (x == nullptr || l == nullptr) return fail(ctx, QDC_EINVAL, "x and l are required");
+    if (ld_l < n || ld_x < width || l_batch < 0 || x_batch < 0)
+        return fail(ctx, QDC_EINVAL, "bad strides ld_l=%lld ld_x=%lld", (long long)ld_l, (long long)ld_x);
+    if (batch > 0x7fffffffLL) return fail(ctx, QDC_EINVAL, "batch %lld too large", (long long)batch);
+    const int64_t tiles = (width + qdc::kTriThreads - 1) / qdc::kTriThreads;
+    if (tiles > 65535) return fail(ctx, QDC_EINVAL, "width %lld too large", (long long)width);
+    DeviceGuard guard(ctx->device);
+    if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
+    qdc::TriSolveArgs a{x, l, ld_l, l_batch, ld_x, x_batch, width, n};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(batch), unsigned(tiles));
+    cfg.blockDim = dim3(unsigned(qdc::kTriThreads));
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = ctx->pdl ? attr : nullptr;
+    cfg.numAttrs = ctx->pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, qdc::unit_lower_solve, a);
+    if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch unit_lower_solve: %s", cudaGetErrorString(e));
+    return QDC_OK;
+}
+
 // ------------------------------------------------------------------ SwiGLU
 
 int qdc_swiglu(qdc_ctx* ctx, float* out_f32, uint16_t* out_bf16, const float* g, const float* u,

@@ -1218,4 +1218,61 @@ static __global__ void __launch_bounds__(kThreads) swiglu_generic(SwigluArgs a) 
     }
 }
 
+// ------------------------------------------- unit lower-triangular solve
+// X_b <- (I + strict_lower(L_b))^{-1} X_b for a batch of n x n matrices
+// (n <= 64): the chunked gated delta rule's UnitLowerTriangular(system) \ rhs
+// (src/backbone.jl:279, ext/QwenDecisionCoreCUDAExt.jl:22-24), solved in
+// place so that the forward needs no solver workspace.  One CTA per (matrix,
+// 128-column tile): the strict lower triangle of L and the tile of X go to
+// shared memory; each thread forward-substitutes its own column,
+//   x_i = x_i - sum_{k<i} L_ik x_k   (k ascending, one FMA chain per row),
+// reading row i of L as 16-byte broadcasts and its column of X without bank
+// conflicts (column t sits in bank t mod 32).  The work is small next to the
+// GEMMs around it; a register-resident column (64 values) spilled.
+
+constexpr int kTriMax = 64;
+constexpr int kTriThreads = 128;
+
+struct TriSolveArgs {
+    float* x;
+    const float* l;
+    int64_t ld_l, l_batch, ld_x, x_batch, width;
+    int n;
+};
+
+static __global__ void __launch_bounds__(kTriThreads) unit_lower_solve(TriSolveArgs a) {
+    pdl_enter();
+    __shared__ __align__(16) float ls[kTriMax][kTriMax];
+    __shared__ float xs[kTriMax][kTriThreads];
+    const int t = threadIdx.x;
+    const int n = a.n;
+    const int64_t b = blockIdx.x;
+    const float* l = a.l + b * a.l_batch;
+    for (int e = t; e < n * kTriMax; e += kTriThreads) {
+        const int i = e / kTriMax, k = e % kTriMax;
+        ls[i][k] = k < i ? __ldg(l + int64_t(i) * a.ld_l + k) : 0.0f;
+    }
+    const int64_t col = int64_t(blockIdx.y) * kTriThreads + t;
+    const bool live = col < a.width;
+    float* x = a.x + b * a.x_batch + col;
+    for (int i = 0; i < n; ++i) xs[i][t] = live ? x[int64_t(i) * a.ld_x] : 0.0f;
+    __syncthreads();
+    for (int i = 1; i < n; ++i) {
+        float acc = xs[i][t];
+        const float4* li = reinterpret_cast<const float4*>(ls[i]);
+        int k = 0;
+        for (; k + 4 <= i; k += 4) {
+            const float4 lv = li[k >> 2];
+            acc = __fmaf_rn(-lv.x, xs[k][t], acc);
+            acc = __fmaf_rn(-lv.y, xs[k + 1][t], acc);
+            acc = __fmaf_rn(-lv.z, xs[k + 2][t], acc);
+            acc = __fmaf_rn(-lv.w, xs[k + 3][t], acc);
+        }
+        for (; k < i; ++k) acc = __fmaf_rn(-ls[i][k], xs[k][t], acc);
+        xs[i][t] = acc;
+    }
+    if (live)
+        for (int i = 0; i < n; ++i) x[int64_t(i) * a.ld_x] = xs[i][t];
+}
+
 }  // namespace qdc

@@ -241,6 +241,24 @@ function delta_conv_norm!(query::CUDA.CuArray{Float32,3}, key::CUDA.CuArray{Floa
     return query, key, value
 end
 
+"""delta_solve!(system, rhs)  -- rhs .= UnitLowerTriangular(system) \\ rhs in place
+for one (n, n) system (n <= 64) or a batch (n, n, batch) / (width, n, batch)
+-- the delta_solve hook of the chunked gated delta rule (src/backbone.jl:279,
+ext/QwenDecisionCoreCUDAExt.jl:22-24) with no solver workspace.  A Julia
+column-major (n, n) system is the row-major transpose, so the library sees
+rhs' as (n rows x width) and system' as its upper triangle: pass
+`transpose`d copies, or use the row-major layout throughout."""
+function delta_solve!(system::CUDA.CuArray{Float32}, rhs::CUDA.CuArray{Float32}; n::Integer,
+                      width::Integer, batch::Integer = 1)
+    ctx = context()
+    check(ccall((:qdc_unit_lower_solve, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Cint, Int64, Int64, Int64, Int64, Int64,
+                 Ptr{Cvoid}),
+                ctx.handle, ptr(rhs), ptr(system), Int64(batch), Cint(n), Int64(width), Int64(n),
+                Int64(n * n), Int64(width), Int64(n * width), stream_handle()), ctx.handle)
+    return rhs
+end
+
 """upload_bf16(bits::Array{UInt16}) -> CuArray{Float32}: a checkpoint's raw
 BF16 words copied to the device as they are and widened there (bits << 16,
 src/safetensors.jl:28-30), half the host -> device bytes of widening on the
@@ -395,7 +413,8 @@ function __init__()
                                                           qk_norm_rope!,
                                                           q_k_norm_rope!, rope_tables, gated_rms!,
                                                           swiglu!, attn_gate!, delta_gates!,
-                                                          delta_conv_norm!, upload_bf16, to_bf16!,
+                                                          delta_conv_norm!, delta_solve!,
+                                                          upload_bf16, to_bf16!,
                                                           set_pdl!, ws_reserve!, ws_reset!,
                                                           ws_mark, ws_release!, ws_stats,
                                                           scratch, sync!))

@@ -81,6 +81,7 @@ SIGNATURES = {
     "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
                             _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],
+    "qdc_unit_lower_solve": [_vp, _vp, _vp, _i64, _int, _i64, _i64, _i64, _i64, _i64, _vp],
 }
 _RESTYPES = {"qdc_status_string": ctypes.c_char_p, "qdc_last_error": ctypes.c_char_p}
 

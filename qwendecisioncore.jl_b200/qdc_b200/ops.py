@@ -20,6 +20,9 @@ for CuArrays and the work done by the library's sm_100a kernels:
   native_delta_gates   beta / decay of delta_attention, src/backbone.jl:292-297,
                        ext/cuda_delta.jl:168-181
   native_mlp_gate      src/backbone.jl:352-355, ext/cuda_mlp.jl:49-61
+  native_delta_solve   delta_solve (UnitLowerTriangular(system) \\ rhs) of the
+                       chunked gated delta rule, src/backbone.jl:279,
+                       ext/QwenDecisionCoreCUDAExt.jl:22-24
   native_bf16_to_f32   BF16 decode (bits << 16), src/safetensors.jl:28-30
   native_f32_to_bf16   BF16 encode (round to nearest even), src/safetensors.jl:38-42
   rope_table           src/backbone_cpu.jl:90-105
@@ -118,6 +121,10 @@ class Context:
             numel *= int(s)
         nbytes = numel * torch.empty((), dtype=dtype).element_size()
         ptr = self.ws_alloc(max(nbytes, 1))
+        return self.wrap(ptr, shape, dtype)
+
+    def wrap(self, ptr, shape, dtype=torch.float32):
+        """A tensor view of `shape` over device memory at `ptr` (not owned)."""
         return _wrap_device_pointer(ptr, tuple(int(s) for s in shape), dtype, self.device)
 
 
@@ -134,7 +141,7 @@ def context(device=None):
 
 
 _TORCH_TYPESTR = {torch.float32: "<f4", torch.bfloat16: "<u2", torch.int32: "<i4",
-                  torch.uint8: "|u1", torch.int64: "<i8"}
+                  torch.uint8: "|u1", torch.int64: "<i8", torch.bool: "|b1"}
 
 
 class _CudaArray:
@@ -607,3 +614,28 @@ def native_mlp_gate(gate, up, *, want_f32=True, want_bf16=False, out_f32=None, o
         check(ctx.lib.qdc_swiglu(ctx.handle, _ptr(out_f32), _ptr(out_bf16), _ptr(gate), _ptr(up),
                                  rows, width, ld_g, ld_u, ld_out, _stream(dev, stream)), ctx.handle)
     return out_f32, out_bf16
+
+
+def native_delta_solve(system, x, *, ctx=None, stream=None):
+    """x <- UnitLowerTriangular(system) \\ x in place for a batch (delta_solve,
+    src/backbone.jl:279): system (batch, n, n) and x (batch, n, width)
+    Float32 views with unit inner stride, n <= 64; the diagonal and upper
+    triangle of system are not read.  Returns x."""
+    dev = _cuda(system, x)
+    if system.dim() != 3 or x.dim() != 3 or system.shape[0] != x.shape[0] \
+            or system.shape[1] != system.shape[2] or x.shape[1] != system.shape[1]:
+        raise DimensionMismatch(_lib.QDC_EINVAL, "system (batch, n, n) and x (batch, n, width) expected")
+    if system.dtype != torch.float32 or x.dtype != torch.float32:
+        raise ArgumentError(_lib.QDC_EINVAL, "delta_solve takes Float32 tensors")
+    batch, n, width = x.shape
+    if x.numel() == 0:
+        return x
+    for t, name in ((system, "system"), (x, "x")):
+        if t.shape[2] > 1 and t.stride(2) != 1:
+            raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} needs a unit inner stride")
+    ctx = ctx or context(dev)
+    with ctx.lock:
+        check(ctx.lib.qdc_unit_lower_solve(ctx.handle, _ptr(x), _ptr(system), batch, n, width,
+                                           system.stride(1), system.stride(0), x.stride(1), x.stride(0),
+                                           _stream(dev, stream)), ctx.handle)
+    return x

@@ -60,6 +60,49 @@ def test_fixture_logits(q, fixture_model, readout, name):
     assert worst <= 1.0
 
 
+def test_forward_runs_in_the_workspace(q, readout):
+    """The forward's memory is the model's libqdc_b200 workspace arena
+    (ext/cuda_workspace.jl:4-87): after warm-up, an all-token forward and a
+    graphed last-token forward make no torch device allocation (the caching
+    allocator's allocation and segment counts do not move), the arena
+    neither grows nor moves, every kernel output is a slot of the arena,
+    and the results still match the reference's golden logits."""
+    model = q.QwenBackbone.from_directory(GOLDEN, device="cuda")
+    with open(os.path.join(GOLDEN, "reference.json")) as f:
+        samples = json.load(f)
+    for sample in samples[2:]:
+        ids_rows, mask_rows = sample["inputs"]["input_ids"], sample["inputs"]["attention_mask"]
+        expected = np.array(sample["logits"], np.float64)
+        for r, (ids, mask) in enumerate(zip(ids_rows, mask_rows)):
+            for _ in range(2):  # warm-up: arena size, slot views, cuBLAS workspaces, masks, graph
+                q.backbone_hidden(model, ids, mask)
+                q.backbone_last_hidden(model, ids, mask)
+            torch.cuda.synchronize()
+            before = torch.cuda.memory_stats()
+            arena = (model.ws.generation, model.ws.capacity)
+            states = q.backbone_hidden(model, ids, mask)
+            last = q.backbone_last_hidden(model, ids, mask)
+            torch.cuda.synchronize()
+            after = torch.cuda.memory_stats()
+            for key in ("allocation.all.allocated", "segment.all.allocated"):
+                assert after[key] == before[key], (key, before[key], after[key])
+            assert (model.ws.generation, model.ws.capacity) == arena
+            assert _violation(readout @ states[-1].astype(np.float64), expected[r]) <= 1.0
+            assert _violation(readout @ last.astype(np.float64), expected[r]) <= 1.0
+    model.trace, model.trace_ptrs = [], []
+    try:
+        model.batch_hidden(np.array(samples[-1]["inputs"]["input_ids"]),
+                           np.array(samples[-1]["inputs"]["attention_mask"]))
+        ptrs = model.trace_ptrs
+    finally:
+        model.trace = None
+    assert len(ptrs) >= 10
+    base = model.ws._base
+    for site, outs in ptrs:
+        for p in outs:
+            assert base <= p < base + model.ws.capacity, site
+
+
 def test_last_hidden_graph_replay(q, fixture_model, monkeypatch):
     """The cached CUDA graph of the last-token forward (test/cuda.jl:17-28,
     48-65): captured, replayed on changed values at a fixed shape, equal to
@@ -243,7 +286,7 @@ def check_every_site(model, trace, ids, S, oracle):
 
 def traced_forward(model, ids, mask=None):
     """batch_hidden of (B, S) ids with every per-layer kernel call recorded."""
-    model.trace = []
+    model.trace, model.trace_ptrs = [], []
     try:
         out = model.batch_hidden(ids, mask)
         return out, model.trace
@@ -290,6 +333,9 @@ def test_0p8b_every_kernel_site_2048_tokens(model_0p8b, oracle):
     MLP residual + next norm, the final norm) against the oracle."""
     ids = np.random.default_rng(2048).integers(0, 151936, (1, 2048))
     _, trace = traced_forward(model_0p8b, ids)
+    base, cap = model_0p8b.ws._base, model_0p8b.ws.capacity
+    for site, outs in model_0p8b.trace_ptrs:  # every kernel output is a workspace slot
+        assert all(base <= p < base + cap for p in outs), site
     # gather; conv, gates, gated norm per DeltaNet layer; q, k, gate per
     # attention layer; post norm, SwiGLU, residual + next norm per layer
     assert check_every_site(model_0p8b, trace, ids.reshape(-1), 2048, oracle) == 1 + 18 * 3 + 6 * 3 + 24 * 3
@@ -318,7 +364,12 @@ def test_0p8b_short_sequence_with_holes(model_0p8b, oracle):
     omodel = F.Model(F.Config(**{k: getattr(cfg, k) for k in F.Config.__dataclass_fields__}), weights)
     expected = F.backbone_hidden(omodel, ids[0], mask[0])
     del weights, omodel
+    q_hidden(model_0p8b, ids[0], mask[0])  # warm-up at this shape
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_stats()["allocation.all.allocated"]
     actual = q_hidden(model_0p8b, ids[0], mask[0])
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats()["allocation.all.allocated"] == before  # the forward allocates nothing
     assert _violation(actual.astype(np.float64), expected.astype(np.float64)) <= 24 / 4
 
 

@@ -692,3 +692,36 @@ def test_delta_conv_norm_negative_zero_window(q, oracle):
         a = got.cpu().numpy()
         assert np.array_equal(a, exp) and np.array_equal(np.signbit(a), np.signbit(exp))
         assert not np.signbit(exp).any()
+
+
+@pytest.mark.parametrize("batch,n,width,ld_pad", [(300, 64, 256, 0), (7, 64, 128, 64), (5, 17, 100, 3),
+                                                  (3, 1, 5, 0), (2, 64, 1, 0), (1, 33, 300, 0)])
+def test_delta_solve(q, oracle, batch, n, width, ld_pad):
+    """delta_solve in place (UnitLowerTriangular(system) \\ rhs,
+    src/backbone.jl:279) against the oracle's forward substitution, with
+    the right-hand side a column slice of a wider buffer (as the chunked
+    delta rule solves [V*beta | K*beta*exp(cum)] in one go) and garbage on
+    and above the diagonal of system, which must not be read.  Entries
+    of system in [-0.3, 0.3] (the delta rule's are beta * k_i.k_j * decay,
+    at most 1 in magnitude)."""
+    rng = np.random.default_rng(batch * n + width)
+    system = rng.uniform(-0.3, 0.3, (batch, n, n)).astype(np.float32)
+    system += np.triu(np.full((n, n), 7.0, np.float32))
+    rhs = rng.standard_normal((batch, n, width + ld_pad), dtype=np.float32)
+    expected = oracle.unit_lower_solve(system, np.ascontiguousarray(rhs[:, :, :width]))
+    dsys = torch.from_numpy(system).cuda()
+    drhs = torch.from_numpy(rhs).cuda()
+    got = q.native_delta_solve(dsys, drhs[:, :, :width])
+    scale = np.abs(expected).max(axis=1, keepdims=True) + 1e-30
+    a = got.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(a - expected) <= 1e-5 * scale + 1e-6)
+    assert np.array_equal(drhs[:, :, width:].cpu().numpy(), rhs[:, :, width:])  # pad untouched
+    assert np.array_equal(dsys.cpu().numpy(), system)
+
+
+def test_delta_solve_rejects_bad_arguments(q):
+    x = torch.zeros((2, 65, 8), device="cuda")
+    with pytest.raises(q.ArgumentError):
+        q.native_delta_solve(torch.zeros((2, 65, 65), device="cuda"), x)
+    with pytest.raises(q.DimensionMismatch):
+        q.native_delta_solve(torch.zeros((2, 4, 4), device="cuda"), torch.zeros((2, 5, 8), device="cuda"))

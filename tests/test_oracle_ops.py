@@ -267,3 +267,16 @@ def test_attn_gate_ramps(oracle, B, S, H, D):
     v = values.astype(np.float64).transpose(0, 2, 1, 3).reshape(B * S, H, D)
     exp = v / (1.0 + np.exp(-gate.astype(np.float64)))
     assert close(got.reshape(B * S, H, D), exp)
+
+
+def test_unit_lower_solve_matches_float64(oracle):
+    """The oracle's delta_solve (forward substitution in Float32) against a
+    float64 solve with the unit lower triangle of the same matrices."""
+    rng = np.random.default_rng(3)
+    for n, width in ((64, 256), (17, 3), (1, 4)):
+        L = rng.uniform(-0.3, 0.3, (4, n, n)).astype(np.float32)
+        L += np.triu(np.full((n, n), 9.0, np.float32))  # never read
+        R = rng.standard_normal((4, n, width)).astype(np.float32)
+        x = oracle.unit_lower_solve(L, R)
+        exact = np.linalg.solve(np.tril(L.astype(np.float64), -1) + np.eye(n), R.astype(np.float64))
+        assert np.all(np.abs(x - exact) <= 1e-5 * np.abs(exact).max(axis=1, keepdims=True) + 1e-6)

@@ -485,23 +485,31 @@ def test_capture_survives_other_threads_cuda_work(q):
 
 
 @pytest.mark.parametrize("B,S,Hk,Hv", [(1, 130, 2, 4), (4, 256, 4, 16), (8, 65, 2, 8)])
-def test_chunked_delta_forms_agree_on_gpu(B, S, Hk, Hv):
+def test_chunked_delta_forms_agree_on_gpu(q, B, S, Hk, Hv):
     """The two hand-off forms of the chunked delta rule (linear scan and per
-    chunk) give the same outputs on the GPU."""
-    from qdc_b200.backbone import chunked_delta
+    chunk), every intermediate in its own slot and the solve by the qdc
+    kernel, give the same outputs on the GPU."""
+    from qdc_b200.backbone import _chunked_spec, chunked_delta
     g = torch.Generator(device="cuda").manual_seed(B * S + Hv)
     Dk, Dv = 128, 128
     kw = dict(device="cuda", generator=g)
-    q = torch.nn.functional.normalize(torch.randn(B, S, Hk, Dk, **kw), dim=-1) / Dk ** 0.5
+    qq = torch.nn.functional.normalize(torch.randn(B, S, Hk, Dk, **kw), dim=-1) / Dk ** 0.5
     k = torch.nn.functional.normalize(torch.randn(B, S, Hk, Dk, **kw), dim=-1)
     v = torch.randn(B, S, Hv, Dv, **kw)
     beta = torch.rand(B, S, Hv, **kw)
     decay = -torch.rand(B, S, Hv, **kw)
+    upper = torch.ones((64, 64), dtype=torch.bool, device="cuda").triu_(1)
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
+    outs = []
     try:
-        a = chunked_delta(q, k, v, beta, decay, Hv // Hk, scan=True).double()
-        b = chunked_delta(q, k, v, beta, decay, Hv // Hk, scan=False).double()
+        for scan in (True, False):
+            slots = {name: torch.full(shape, float("nan"), device="cuda").to(dt)
+                     for name, (shape, dt) in _chunked_spec(B, S, Hv, Dk, Dv, scan).items()}
+            out = torch.full((B, S, Hv, Dv), float("nan"), device="cuda")
+            chunked_delta(qq, k, v, beta, decay, Hv // Hk, slots, out, upper, q.native_delta_solve)
+            outs.append(out.double())
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+    a, b = outs
     assert torch.all((a - b).abs() <= TOL + TOL * b.abs())

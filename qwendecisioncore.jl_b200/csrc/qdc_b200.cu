@@ -111,27 +111,35 @@ int qdc_resident_blocks(const void* kernel, int device, int threads) {
     return n;
 }
 
+// Persistent grid of at most one full wave (shared with qdc_noalloc.cu).
+// When the work takes three or more grid-stride rounds at full occupancy,
+// every resident slot is used: the extra warps keep more bytes in flight and
+// the kernel stays bandwidth-bound through a ragged last round (measured on
+// B200, chains of residual-norm launches: 6.11 TB/s and 1.9 us fixed per
+// launch, against 6.03 TB/s and 2.3 us for grids trimmed to equal rounds).
+// With one or two rounds the grid is trimmed so that every round is full
+// (4,096 rows: 12.7 us against 12.9).
+int64_t qdc_grid_size(int64_t cap, int64_t work_per_block_units, int64_t units) {
+    if (units < 1) units = 1;
+    if (work_per_block_units < 1) work_per_block_units = 1;
+    const int64_t per_wave = cap * work_per_block_units;
+    const int64_t rounds = (units + per_wave - 1) / per_wave;
+    if (rounds >= 3) return cap;
+    const int64_t per_block = rounds * work_per_block_units;
+    int64_t g = (units + per_block - 1) / per_block;
+    if (g > cap) g = cap;
+    return g < 1 ? 1 : g;
+}
+
 namespace {
 
 int resident_blocks(const void* kernel, int device, int threads) {
     return qdc_resident_blocks(kernel, device, threads);
 }
 
-// Persistent grid of at most one full wave, balanced: with R grid-stride
-// rounds needed at full occupancy, launch just enough CTAs that every round
-// is full except the last few units, so no round runs with a fraction of the
-// warps (at 8192 rows a full wave of 3552 warps would leave the third round
-// 31% busy).
 int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units) {
-    if (units < 1) units = 1;
-    if (work_per_block_units < 1) work_per_block_units = 1;
     const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, qdc::kThreads);
-    const int64_t per_wave = cap * work_per_block_units;
-    const int64_t rounds = (units + per_wave - 1) / per_wave;
-    const int64_t per_block = rounds * work_per_block_units;
-    int64_t g = (units + per_block - 1) / per_block;
-    if (g > cap) g = cap;
-    return int(g < 1 ? 1 : g);
+    return int(qdc_grid_size(cap, work_per_block_units, units));
 }
 
 // Launch, with programmatic stream serialization when the context turned it
@@ -691,20 +699,24 @@ int qdc_delta_gates(qdc_ctx* ctx, float* beta, float* decay, const float* proj, 
 
 // ------------------------------------------------------- DeltaNet prologue
 
-int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj,
-                        int64_t ld_proj, const float* conv_w, int64_t tokens, int64_t seq_len,
-                        int key_heads, int key_dim, int value_heads, int value_dim, float eps,
-                        void* stream) {
-    if (int s = check_ctx(ctx)) return s;
-    if (tokens < 0 || key_heads < 1 || key_dim < 1 || value_heads < 1 || value_dim < 1 || seq_len < 0)
-        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d/%d dims=%d/%d", (long long)tokens,
-                    key_heads, value_heads, key_dim, value_dim);
-    const int64_t channels = 2 * int64_t(key_heads) * key_dim + int64_t(value_heads) * value_dim;
-    if (ld_proj < channels)
-        return fail(ctx, QDC_EINVAL, "ld_proj %lld < %lld channels", (long long)ld_proj, (long long)channels);
-    if (tokens == 0) return QDC_OK;
-    if (!q_out || !k_out || !v_out || !proj || !conv_w)
-        return fail(ctx, QDC_EINVAL, "outputs, proj and conv_w are required");
+}  // extern "C"
+
+namespace {
+
+struct GateOut {
+    float* beta = nullptr;
+    float* decay = nullptr;
+    const float* a_decay = nullptr;
+    const float* dt_bias = nullptr;
+    int64_t start = 0;
+};
+
+// Conv + SiLU + q/k L2 norms, and with `gates.beta` set the beta / decay
+// gates too: fused into the shared-memory pipeline when it applies, else a
+// separate gates launch.  Arguments are validated by the callers.
+int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj, int64_t ld_proj,
+              const float* conv_w, int64_t tokens, int64_t seq_len, int key_heads, int key_dim,
+              int value_heads, int value_dim, float eps, const GateOut& gates, void* stream) {
     const int64_t per_tok = 2 * int64_t(key_heads) + value_heads;
     DeviceGuard guard(ctx->device);
     if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
@@ -728,7 +740,8 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
         }
         qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                         value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),
-                        make_fastdiv(uint32_t(groups)), seq_div};
+                        make_fastdiv(uint32_t(groups)), seq_div, gates.beta, gates.decay, gates.a_decay,
+                        gates.dt_bias, gates.start};
         const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
         return launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
                       size_t(smem));
@@ -739,16 +752,84 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
                      runs * per_tok < (int64_t(1) << 32) - (int64_t(1) << 24);
     qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                     value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)),
-                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div};
+                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div,
+                    nullptr, nullptr, nullptr, nullptr, 0};
+    int st;
     if (vec) {
         auto k = qdc::delta_conv_norm_vec<R>;
         const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32,
                                   runs * per_tok);
-        return launch(ctx, k, grid, a, stream, "delta_conv_norm");
+        st = launch(ctx, k, grid, a, stream, "delta_conv_norm");
+    } else {
+        auto k = qdc::delta_conv_norm_generic;
+        const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
+        st = launch(ctx, k, grid, a, stream, "delta_conv_norm");
     }
-    auto k = qdc::delta_conv_norm_generic;
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
-    return launch(ctx, k, grid, a, stream, "delta_conv_norm");
+    if (st != QDC_OK || gates.beta == nullptr) return st;
+    return qdc_delta_gates(ctx, gates.beta, gates.decay, proj, ld_proj, gates.start, gates.a_decay, gates.dt_bias,
+                           tokens, value_heads, stream);
+}
+
+int conv_checks(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj, int64_t ld_proj,
+                const float* conv_w, int64_t tokens, int64_t seq_len, int key_heads, int key_dim,
+                int value_heads, int value_dim) {
+    if (tokens < 0 || key_heads < 1 || key_dim < 1 || value_heads < 1 || value_dim < 1 || seq_len < 0)
+        return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d/%d dims=%d/%d", (long long)tokens,
+                    key_heads, value_heads, key_dim, value_dim);
+    const int64_t channels = 2 * int64_t(key_heads) * key_dim + int64_t(value_heads) * value_dim;
+    if (ld_proj < channels)
+        return fail(ctx, QDC_EINVAL, "ld_proj %lld < %lld channels", (long long)ld_proj, (long long)channels);
+    if (tokens == 0) return QDC_OK;
+    if (!q_out || !k_out || !v_out || !proj || !conv_w)
+        return fail(ctx, QDC_EINVAL, "outputs, proj and conv_w are required");
+    return QDC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj,
+                        int64_t ld_proj, const float* conv_w, int64_t tokens, int64_t seq_len,
+                        int key_heads, int key_dim, int value_heads, int value_dim, float eps,
+                        void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (int s = conv_checks(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads,
+                            key_dim, value_heads, value_dim))
+        return s;
+    if (tokens == 0) return QDC_OK;
+    return conv_impl(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads, key_dim,
+                     value_heads, value_dim, eps, GateOut{}, stream);
+}
+
+int qdc_delta_prologue(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, float* beta, float* decay,
+                       const float* proj, int64_t ld_proj, const float* conv_w, int64_t gate_start,
+                       const float* a_decay, const float* dt_bias, int64_t tokens, int64_t seq_len,
+                       int key_heads, int key_dim, int value_heads, int value_dim, float eps, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (int s = conv_checks(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads,
+                            key_dim, value_heads, value_dim))
+        return s;
+    const int64_t channels = 2 * int64_t(key_heads) * key_dim + int64_t(value_heads) * value_dim;
+    if (gate_start < 0 || ld_proj < gate_start + 2 * int64_t(value_heads))
+        return fail(ctx, QDC_EINVAL, "gate columns [%lld, %lld) fall outside ld_proj %lld",
+                    (long long)gate_start, (long long)(gate_start + 2 * int64_t(value_heads)), (long long)ld_proj);
+    if (gate_start < channels)
+        return fail(ctx, QDC_EINVAL, "gate columns start at %lld, inside the %lld conv channels",
+                    (long long)gate_start, (long long)channels);
+    if (tokens == 0) return QDC_OK;
+    if (!beta || !decay || !a_decay || !dt_bias)
+        return fail(ctx, QDC_EINVAL, "beta, decay, a_decay and dt_bias are required");
+    if (tokens * value_heads >= (int64_t(1) << 32) - (int64_t(1) << 24))
+        return fail(ctx, QDC_EINVAL, "too many (token, head) units");
+    GateOut g;
+    g.beta = beta;
+    g.decay = decay;
+    g.a_decay = a_decay;
+    g.dt_bias = dt_bias;
+    g.start = gate_start;
+    return conv_impl(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads, key_dim,
+                     value_heads, value_dim, eps, g, stream);
 }
 
 // ------------------------------------------------------- bf16 <-> Float32

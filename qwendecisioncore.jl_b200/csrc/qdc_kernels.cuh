@@ -673,6 +673,14 @@ struct ConvArgs {
     uint32_t units;      // vector path: runs * heads; generic: tokens * heads
     FastDiv heads_div;   // 2 kh + vh
     FastDiv seq_div;     // seq_len (tokens when unset)
+    // optional DeltaNet gates (pipeline kernel only; beta NULL: none):
+    // a of token t, value head h at proj[t*ld + gate_start + h], b at
+    // proj[t*ld + gate_start + vh + h]; beta, decay dense [tokens][vh]
+    float* beta;
+    float* decay;
+    const float* a_decay;
+    const float* dt_bias;
+    int64_t gate_start;
 };
 
 struct ConvHead {
@@ -782,6 +790,20 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 constexpr int kConvPipeThreads = 768;
 
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)) (src/backbone.jl:198) with the
+// library's expf / log1pf (a few ulp).
+__device__ __forceinline__ float softplus(float x) {
+    return __fadd_rn(fmaxf(x, 0.0f), log1pf(expf(-fabsf(x))));
+}
+
+// beta = inv(1 + exp(-b)) and decay = a_decay * softplus(a + dt_bias) of one
+// (token, value head), src/backbone.jl:292-297.
+__device__ __forceinline__ void delta_gate(float a, float b, float a_decay, float dt_bias, float* beta,
+                                           float* decay) {
+    *beta = __frcp_rn(__fadd_rn(1.0f, expf(-b)));
+    *decay = __fmul_rn(a_decay, softplus(__fadd_rn(a, dt_bias)));
+}
+
 template <int R, int STAGES>
 __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(ConvArgs a) {
     pdl_enter();
@@ -816,15 +838,41 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
     }
     const int hq = warp & 3;
     const int r0 = (warp >> 2) * TPW;
+    // gates: the value heads of a run are spread over the run's head groups,
+    // hpg heads per group, one (token, head) per thread (R * hpg <= threads)
+    const int hpg = a.beta ? (a.vh + int(groups) - 1) / int(groups) : 0;
     int stage = 0;
     for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         const uint32_t ahead = tile + uint32_t(STAGES - 1) * gridDim.x;
         if (ahead < tiles) issue(ahead, (stage + STAGES - 1) % STAGES);
         cp_async_commit();
-        cp_async_wait<STAGES - 1>();  // this tile's copies have landed
-        __syncthreads();
         const uint32_t run = fdiv(tile, a.heads_div);
         const uint32_t g = tile - run * groups;
+        // this tile's gate inputs, loaded while its copies land
+        int gate_h = -1;
+        int64_t gate_t = 0;
+        float ga = 0.0f, gb = 0.0f, gad = 0.0f, gdt = 0.0f;
+        if (hpg > 0) {
+            const int h0 = int(g) * hpg;
+            const int nh = a.vh - h0 < hpg ? a.vh - h0 : hpg;
+            if (nh > 0 && tid < R * nh) {
+                gate_t = int64_t(run) * R + tid / nh;
+                if (gate_t < a.tokens) {
+                    gate_h = h0 + tid % nh;
+                    const float* row = a.proj + gate_t * a.ld + a.gate_start;
+                    ga = __ldg(row + gate_h);
+                    gb = __ldg(row + a.vh + gate_h);
+                    gad = __ldg(a.a_decay + gate_h);
+                    gdt = __ldg(a.dt_bias + gate_h);
+                }
+            }
+        }
+        cp_async_wait<STAGES - 1>();  // this tile's copies have landed
+        __syncthreads();
+        if (gate_h >= 0) {
+            const int64_t o = gate_t * a.vh + gate_h;
+            delta_gate(ga, gb, gad, gdt, a.beta + o, a.decay + o);
+        }
         const ConvHead h = conv_head(a, int(g * 4 + hq));
         const int64_t c = h.c0 + lane * 4;
         float4 wt[4];  // taps 0..3 of channels c..c+3
@@ -1052,12 +1100,6 @@ struct DeltaGateArgs {
     FastDiv heads_div;
 };
 
-// softplus(x) = max(x, 0) + log1p(exp(-|x|)) (src/backbone.jl:198) with the
-// library's correctly rounded-to-a-few-ulp expf / log1pf.
-__device__ __forceinline__ float softplus(float x) {
-    return __fadd_rn(fmaxf(x, 0.0f), log1pf(expf(-fabsf(x))));
-}
-
 // One thread per (token, head): consecutive threads read consecutive
 // columns of a token's a / b group and write consecutive outputs.
 static __global__ void __launch_bounds__(kThreads) delta_gates(DeltaGateArgs a) {
@@ -1067,10 +1109,8 @@ static __global__ void __launch_bounds__(kThreads) delta_gates(DeltaGateArgs a) 
         const uint32_t t = fdiv(i, a.heads_div);
         const int h = int(i - t * uint32_t(a.heads));
         const float* row = a.proj + int64_t(t) * a.ld + a.start;
-        const float x = __fadd_rn(__ldg(row + h), __ldg(a.dt_bias + h));
-        const float b = __ldg(row + a.heads + h);
-        a.beta[i] = __frcp_rn(__fadd_rn(1.0f, expf(-b)));
-        a.decay[i] = __fmul_rn(__ldg(a.a_decay + h), softplus(x));
+        delta_gate(__ldg(row + h), __ldg(row + a.heads + h), __ldg(a.a_decay + h), __ldg(a.dt_bias + h),
+                   a.beta + i, a.decay + i);
     }
 }
 

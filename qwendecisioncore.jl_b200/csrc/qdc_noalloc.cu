@@ -46,9 +46,10 @@
 static __device__ __align__(256) int32_t g_noalloc_ids[QDC_NOALLOC_MAX_IDS];
 
 // Defined in qdc_b200.cu (not exported): the per-thread text that
-// qdc_last_error(NULL) returns, and the cached occupancy query.
+// qdc_last_error(NULL) returns, the cached occupancy query and the grid rule.
 void qdc_set_thread_error(const char* msg);
 int qdc_resident_blocks(const void* kernel, int device, int threads);
+int64_t qdc_grid_size(int64_t cap, int64_t work_per_block_units, int64_t units);
 
 namespace {
 
@@ -125,15 +126,12 @@ extern "C" int qdc_gather_rms_noalloc(void* out_x, void* out_y, const void* tabl
                      aligned16(gamma) && (hidden * esz) % 16 == 0;
     const qdc::RowKernel k = dtype == QDC_F32 ? qdc::row_kernel_for<float>(hidden, vec)
                                               : qdc::row_kernel_for<uint16_t>(hidden, vec);
-    // persistent grid of at most one wave, every grid-stride round full
-    const int64_t warps = qdc::kThreads / 32;
+    // persistent grid of at most one wave (the context path's rule)
     const int64_t cap = int64_t(s.sm_count) *
                         qdc_resident_blocks(reinterpret_cast<const void*>(k), device, qdc::kThreads);
-    const int64_t rounds = (n + cap * warps - 1) / (cap * warps);
-    int64_t grid = (n + rounds * warps - 1) / (rounds * warps);
-    if (grid > cap) grid = cap;
+    const int64_t grid = qdc_grid_size(cap, qdc::kThreads / 32, n);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(grid < 1 ? 1 : grid));
+    cfg.gridDim = dim3(unsigned(grid));
     cfg.blockDim = dim3(unsigned(qdc::kThreads));
     cfg.stream = st;
     e = cudaLaunchKernelEx(&cfg, k, a);

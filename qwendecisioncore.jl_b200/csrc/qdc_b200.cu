@@ -22,7 +22,7 @@ struct qdc_ctx {
     int device = -1;
     int sm_count = 0;
     bool pdl = false;  // QDC_OPT_PDL
-    bool conv_smem_set = false;  // DeltaNet pipeline's dynamic shared memory limit raised
+    int conv_smem = 0;  // DeltaNet pipeline's dynamic shared memory limit, as raised
     std::string err;
     // workspace arena
     char* arena = nullptr;
@@ -60,6 +60,8 @@ int cuda_fail(qdc_ctx* ctx, cudaError_t e, const char* what) {
     } while (0)
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDynamicSmem = 227 * 1024;  // per CTA on sm_100a
 
 // Multiplier and shift of qdc::FastDiv for divisor d >= 1.
 qdc::FastDiv make_fastdiv(uint32_t d) {
@@ -732,19 +734,35 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
     if (aligned && key_dim == 128 && value_dim == 128 && per_tok % 4 == 0 &&
         tiles < (int64_t(1) << 32) - (int64_t(1) << 24)) {
         auto k = qdc::delta_conv_norm_pipe<PR, PS>;
-        const int smem = PS * (PR + 3) * 512 * int(sizeof(float));
-        // once per context (a context is used by one host thread at a time)
-        if (!ctx->conv_smem_set) {
+        const int conv_smem = PS * (PR + 3) * 512 * int(sizeof(float));
+        // the gates ride in the same pipeline stages (2 * value_heads floats
+        // per token, copied in 16-byte pieces) when they fit
+        const int gate_smem = PS * PR * 2 * value_heads * int(sizeof(float));
+        const bool fuse = gates.beta != nullptr && value_heads % 2 == 0 && gates.start % 4 == 0 &&
+                          conv_smem + gate_smem <= kMaxDynamicSmem;
+        const int smem = conv_smem + (fuse ? gate_smem : 0);
+        // raised once per context and size (a context is used by one host
+        // thread at a time)
+        if (ctx->conv_smem < smem) {
             QDC_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            ctx->conv_smem_set = true;
+            ctx->conv_smem = smem;
         }
         qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                         value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),
-                        make_fastdiv(uint32_t(groups)), seq_div, gates.beta, gates.decay, gates.a_decay,
-                        gates.dt_bias, gates.start};
+                        make_fastdiv(uint32_t(groups)), seq_div};
+        if (fuse) {
+            a.beta = gates.beta;
+            a.decay = gates.decay;
+            a.a_decay = gates.a_decay;
+            a.dt_bias = gates.dt_bias;
+            a.gate_start = gates.start;
+        }
         const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-        return launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
-                      size_t(smem));
+        const int st = launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
+                              size_t(smem));
+        if (st != QDC_OK || fuse || gates.beta == nullptr) return st;
+        return qdc_delta_gates(ctx, gates.beta, gates.decay, proj, ld_proj, gates.start, gates.a_decay,
+                               gates.dt_bias, tokens, value_heads, stream);
     }
     constexpr int R = 8;  // tokens per warp-unit on the register path
     const int64_t runs = (tokens + R - 1) / R;
@@ -752,8 +770,7 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
                      runs * per_tok < (int64_t(1) << 32) - (int64_t(1) << 24);
     qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                     value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)),
-                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div,
-                    nullptr, nullptr, nullptr, nullptr, 0};
+                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div};
     int st;
     if (vec) {
         auto k = qdc::delta_conv_norm_vec<R>;

@@ -676,11 +676,11 @@ struct ConvArgs {
     // optional DeltaNet gates (pipeline kernel only; beta NULL: none):
     // a of token t, value head h at proj[t*ld + gate_start + h], b at
     // proj[t*ld + gate_start + vh + h]; beta, decay dense [tokens][vh]
-    float* beta;
-    float* decay;
-    const float* a_decay;
-    const float* dt_bias;
-    int64_t gate_start;
+    float* beta = nullptr;
+    float* decay = nullptr;
+    const float* a_decay = nullptr;
+    const float* dt_bias = nullptr;
+    int64_t gate_start = 0;
 };
 
 struct ConvHead {
@@ -809,8 +809,10 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
     pdl_enter();
     constexpr int CH = 512, ROWS = R + 3, TG = kConvPipeThreads / 32 / 4, TPW = R / TG;
     static_assert(R % TG == 0 && kConvPipeThreads % (CH / 4) == 0, "tile shape");
-    extern __shared__ __align__(16) float stage_buf[];  // [STAGES][ROWS][CH]
+    extern __shared__ __align__(16) float stage_buf[];  // [STAGES][ROWS][CH], then gates [STAGES][R][2 vh]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gate_w = a.beta ? 2 * a.vh : 0;
+    float* gate_buf = stage_buf + STAGES * ROWS * CH;
     const uint32_t groups = uint32_t(2 * a.kh + a.vh) / 4;
     const uint32_t tiles = a.units;  // runs * groups
     auto issue = [&](uint32_t tile, int stage) {
@@ -829,6 +831,17 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
             const int64_t t = t0 + row;
             if (t >= 0 && t < a.tokens) cp_async16(dst + row * CH + col, s_row);
         }
+        // the run's gate columns (a | b, 2 vh floats per token) ride with its
+        // first head group's tile
+        if (gate_w > 0 && g == 0) {
+            const int per_tok = gate_w / 4;  // 16-byte chunks per token
+            float* gdst = gate_buf + stage * (R * gate_w);
+            for (int i = tid; i < R * per_tok; i += kConvPipeThreads) {
+                const int r = i / per_tok, q4 = i - r * per_tok;
+                const int64_t t = int64_t(run) * R + r;
+                if (t < a.tokens) cp_async16(gdst + r * gate_w + q4 * 4, a.proj + t * a.ld + a.gate_start + q4 * 4);
+            }
+        }
     };
 #pragma unroll
     for (int s = 0; s < STAGES - 1; ++s) {
@@ -838,9 +851,6 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
     }
     const int hq = warp & 3;
     const int r0 = (warp >> 2) * TPW;
-    // gates: the value heads of a run are spread over the run's head groups,
-    // hpg heads per group, one (token, head) per thread (R * hpg <= threads)
-    const int hpg = a.beta ? (a.vh + int(groups) - 1) / int(groups) : 0;
     int stage = 0;
     for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         const uint32_t ahead = tile + uint32_t(STAGES - 1) * gridDim.x;
@@ -848,30 +858,19 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         cp_async_commit();
         const uint32_t run = fdiv(tile, a.heads_div);
         const uint32_t g = tile - run * groups;
-        // this tile's gate inputs, loaded while its copies land
-        int gate_h = -1;
-        int64_t gate_t = 0;
-        float ga = 0.0f, gb = 0.0f, gad = 0.0f, gdt = 0.0f;
-        if (hpg > 0) {
-            const int h0 = int(g) * hpg;
-            const int nh = a.vh - h0 < hpg ? a.vh - h0 : hpg;
-            if (nh > 0 && tid < R * nh) {
-                gate_t = int64_t(run) * R + tid / nh;
-                if (gate_t < a.tokens) {
-                    gate_h = h0 + tid % nh;
-                    const float* row = a.proj + gate_t * a.ld + a.gate_start;
-                    ga = __ldg(row + gate_h);
-                    gb = __ldg(row + a.vh + gate_h);
-                    gad = __ldg(a.a_decay + gate_h);
-                    gdt = __ldg(a.dt_bias + gate_h);
-                }
-            }
-        }
         cp_async_wait<STAGES - 1>();  // this tile's copies have landed
         __syncthreads();
-        if (gate_h >= 0) {
-            const int64_t o = gate_t * a.vh + gate_h;
-            delta_gate(ga, gb, gad, gdt, a.beta + o, a.decay + o);
+        if (gate_w > 0 && g == 0) {
+            // beta / decay of the run's tokens, consecutive threads on
+            // consecutive (token, head) outputs
+            const float* gb = gate_buf + stage * (R * gate_w);
+            for (int i = tid; i < R * a.vh; i += kConvPipeThreads) {
+                const int r = i / a.vh, hv = i - r * a.vh;
+                const int64_t t = int64_t(run) * R + r;
+                if (t < a.tokens)
+                    delta_gate(gb[r * gate_w + hv], gb[r * gate_w + a.vh + hv], __ldg(a.a_decay + hv),
+                               __ldg(a.dt_bias + hv), a.beta + t * a.vh + hv, a.decay + t * a.vh + hv);
+            }
         }
         const ConvHead h = conv_head(a, int(g * 4 + hq));
         const int64_t c = h.c0 + lane * 4;

@@ -727,14 +727,15 @@ def test_delta_solve_rejects_bad_arguments(q):
         q.native_delta_solve(torch.zeros((2, 4, 4), device="cuda"), torch.zeros((2, 5, 8), device="cuda"))
 
 
-@pytest.mark.parametrize("tokens,seq_len,kh,kd,vh,vd", [
-    (4100, 2048, 16, 128, 16, 128),   # the 0.8B shape: shared-memory pipeline, gates fused
-    (333, 0, 2, 128, 4, 128),         # pipeline, one sequence, ragged last run
-    (200, 64, 1, 128, 2, 128),        # 2*kh + vh = 4: pipeline with one head group
-    (130, 0, 1, 128, 3, 128),         # 2*kh + vh = 5: register path, gates launched after
-    (97, 40, 2, 64, 4, 32),           # generic path
+@pytest.mark.parametrize("tokens,seq_len,kh,kd,vh,vd,gate_pad", [
+    (4100, 2048, 16, 128, 16, 128, 0),   # the 0.8B shape: shared-memory pipeline, gates fused
+    (333, 0, 2, 128, 4, 128, 0),         # pipeline, one sequence, ragged last run
+    (200, 64, 1, 128, 2, 128, 0),        # 2*kh + vh = 4: pipeline with one head group
+    (150, 0, 2, 128, 4, 128, 1),         # gate columns not 16-byte aligned: pipeline, gates after
+    (130, 0, 1, 128, 3, 128, 0),         # 2*kh + vh = 5: register path, gates launched after
+    (97, 40, 2, 64, 4, 32, 0),           # generic path
 ])
-def test_delta_prologue_equals_conv_norm_plus_gates(q, oracle, tokens, seq_len, kh, kd, vh, vd):
+def test_delta_prologue_equals_conv_norm_plus_gates(q, oracle, tokens, seq_len, kh, kd, vh, vd, gate_pad):
     """qdc_delta_prologue (conv + SiLU + q/k L2 norms and the beta / decay
     gates, one kernel where the pipeline applies) equals qdc_delta_conv_norm
     followed by qdc_delta_gates bit for bit, and the oracle at the bar;
@@ -742,8 +743,8 @@ def test_delta_prologue_equals_conv_norm_plus_gates(q, oracle, tokens, seq_len, 
     the sigmoid."""
     rng = np.random.default_rng(tokens + vh)
     C = 2 * kh * kd + vh * vd
-    start = C + vh * vd
-    proj = rng.standard_normal((tokens, start + 2 * vh + 3), dtype=np.float32)
+    start = C + vh * vd + gate_pad
+    proj = rng.standard_normal((tokens, start + 2 * vh + 4 - gate_pad), dtype=np.float32)
     proj[:, start:start + 2 * vh] = rng.uniform(-30, 30, (tokens, 2 * vh)).astype(np.float32)
     conv = (rng.standard_normal((C, 4), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
     a_decay = (-np.exp(rng.uniform(-1, 0.5, vh))).astype(np.float32)

@@ -744,7 +744,8 @@ def test_delta_prologue_equals_conv_norm_plus_gates(q, oracle, tokens, seq_len, 
     rng = np.random.default_rng(tokens + vh)
     C = 2 * kh * kd + vh * vd
     start = C + vh * vd + gate_pad
-    proj = rng.standard_normal((tokens, start + 2 * vh + 4 - gate_pad), dtype=np.float32)
+    width = (start + 2 * vh + 3) // 4 * 4 + 4  # rows 16-byte aligned
+    proj = rng.standard_normal((tokens, width), dtype=np.float32)
     proj[:, start:start + 2 * vh] = rng.uniform(-30, 30, (tokens, 2 * vh)).astype(np.float32)
     conv = (rng.standard_normal((C, 4), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
     a_decay = (-np.exp(rng.uniform(-1, 0.5, vh))).astype(np.float32)

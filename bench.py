@@ -338,18 +338,6 @@ def single_kernel(name, tokens, device, seed=1):
         return (lambda: q.native_delta_conv_norm(proj, conv, HK, DK, HV, DV, seq_len=SEQ, q_out=qo,
                                                  k_out=ko, v_out=vo, ctx=ctx),
                 2 * T * QKV_W * 4 + QKV_W * 16)
-    if name == "delta_prologue":
-        # conv + SiLU + q/k L2 norms and the beta / decay gates in one call
-        proj = normal((T, PROJ_W))
-        conv = normal((QKV_W, 1, 4), 0.02)
-        a_decay = normal((HV,)).exp_().neg_()
-        dt_bias = normal((HV,))
-        outs = dict(q_out=torch.empty((T, HK, DK), **f), k_out=torch.empty((T, HK, DK), **f),
-                    v_out=torch.empty((T, HV, DV), **f), beta=torch.empty((T, HV), **f),
-                    decay=torch.empty((T, HV), **f))
-        return (lambda: q.native_delta_prologue(proj, conv, Z_OFF + HV * DV, a_decay, dt_bias, HK, DK, HV, DV,
-                                                seq_len=SEQ, ctx=ctx, **outs),
-                2 * T * QKV_W * 4 + QKV_W * 16 + 4 * T * HV * 4)
     if name == "attn_gate":
         # the attention output (B, H, S, D) of B = tokens / SEQ sequences and
         # the gate half of the packed [q;gate] projection
@@ -436,7 +424,6 @@ CONFIG_CASES = [  # (report name, kernel, tokens): the single-kernel workloads
     # the DeltaNet prologue (conv + SiLU + q/k L2 norms) and the attention
     # output gate at config-5 shapes
     ("cfg5_delta_conv_norm", "delta_conv_norm", 32768),
-    ("cfg5_delta_prologue_with_gates", "delta_prologue", 32768),
     ("cfg5_delta_gates", "delta_gates", 32768),
     ("cfg5_attn_gate", "attn_gate", 16384),
     # weight upload: the config-5 embedding table (151936 x 1024) widened
@@ -679,8 +666,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel alone (gather_rms[_bf16], post_rms[_bf16], swiglu, "
                          "swiglu_bf16, swiglu_both, gated_rms, q_norm_rope, k_norm_rope, qk_norm_rope, "
-                         "delta_conv_norm, delta_prologue, attn_gate, delta_gates, bf16_to_f32, "
-                         "f32_to_bf16)")
+                         "delta_conv_norm, attn_gate, delta_gates, bf16_to_f32, f32_to_bf16)")
     ap.add_argument("--tokens", type=int, default=16384, help="rows for --kernel")
     ap.add_argument("--no-forward", action="store_true", help="skip the whole-forward tokens/s leg")
     ap.add_argument("--forward-steps", type=int, default=2)

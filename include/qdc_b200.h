@@ -283,24 +283,6 @@ QDC_API int qdc_delta_conv_norm(qdc_ctx *ctx, float *q_out, float *k_out,
                                 int key_dim, int value_heads, int value_dim,
                                 float eps, void *stream);
 
-/* The whole DeltaNet prologue in one call: qdc_delta_conv_norm, plus the
- * beta / decay gates of qdc_delta_gates (a of token t, value head h at
- * proj[t*ld_proj + gate_start + h], b at proj[t*ld_proj + gate_start +
- * value_heads + h], beta and decay dense [tokens][value_heads]), with
- * gate_start at or past the conv channels.  Where the shared-memory
- * pipeline applies (key_dim == value_dim == 128, 2*key_heads + value_heads a
- * multiple of 4, 16-byte aligned operands) the gates run inside the same
- * kernel, read while the conv tile lands; otherwise as a second launch.
- * Results equal those of the two separate calls bit for bit.  Replaces the
- * prologue of delta_attention (ext/cuda_delta.jl:199-216: causal_depthwise,
- * qk_normalize_kernel! and delta_gates_kernel!). */
-QDC_API int qdc_delta_prologue(qdc_ctx *ctx, float *q_out, float *k_out, float *v_out,
-                               float *beta, float *decay, const float *proj,
-                               int64_t ld_proj, const float *conv_w, int64_t gate_start,
-                               const float *a_decay, const float *dt_bias, int64_t tokens,
-                               int64_t seq_len, int key_heads, int key_dim,
-                               int value_heads, int value_dim, float eps, void *stream);
-
 /* bf16 storage <-> Float32 on the device, n elements, out and in not
  * overlapping.  qdc_bf16_to_f32: out = bits << 16 (src/safetensors.jl:28-30),
  * exact -- the weight upload path: a checkpoint's raw BF16 bytes are copied

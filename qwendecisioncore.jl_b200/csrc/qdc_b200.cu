@@ -61,7 +61,6 @@ int cuda_fail(qdc_ctx* ctx, cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-constexpr int kMaxDynamicSmem = 227 * 1024;  // per CTA on sm_100a
 
 // Multiplier and shift of qdc::FastDiv for divisor d >= 1.
 qdc::FastDiv make_fastdiv(uint32_t d) {
@@ -705,20 +704,11 @@ int qdc_delta_gates(qdc_ctx* ctx, float* beta, float* decay, const float* proj, 
 
 namespace {
 
-struct GateOut {
-    float* beta = nullptr;
-    float* decay = nullptr;
-    const float* a_decay = nullptr;
-    const float* dt_bias = nullptr;
-    int64_t start = 0;
-};
-
-// Conv + SiLU + q/k L2 norms, and with `gates.beta` set the beta / decay
-// gates too: fused into the shared-memory pipeline when it applies, else a
-// separate gates launch.  Arguments are validated by the callers.
+// Conv + SiLU + q/k L2 norms: the shared-memory pipeline when it applies,
+// else the register or scalar kernel.  Arguments are validated by the caller.
 int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj, int64_t ld_proj,
               const float* conv_w, int64_t tokens, int64_t seq_len, int key_heads, int key_dim,
-              int value_heads, int value_dim, float eps, const GateOut& gates, void* stream) {
+              int value_heads, int value_dim, float eps, void* stream) {
     const int64_t per_tok = 2 * int64_t(key_heads) + value_heads;
     DeviceGuard guard(ctx->device);
     if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
@@ -734,15 +724,8 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
     if (aligned && key_dim == 128 && value_dim == 128 && per_tok % 4 == 0 &&
         tiles < (int64_t(1) << 32) - (int64_t(1) << 24)) {
         auto k = qdc::delta_conv_norm_pipe<PR, PS>;
-        const int conv_smem = PS * (PR + 3) * 512 * int(sizeof(float));
-        // the gates ride in the same pipeline stages (2 * value_heads floats
-        // per token, copied in 16-byte pieces) when they fit
-        const int gate_smem = PS * PR * 2 * value_heads * int(sizeof(float));
-        const bool fuse = gates.beta != nullptr && value_heads % 2 == 0 && gates.start % 4 == 0 &&
-                          conv_smem + gate_smem <= kMaxDynamicSmem;
-        const int smem = conv_smem + (fuse ? gate_smem : 0);
-        // raised once per context and size (a context is used by one host
-        // thread at a time)
+        const int smem = PS * (PR + 3) * 512 * int(sizeof(float));
+        // raised once per context (a context is used by one host thread at a time)
         if (ctx->conv_smem < smem) {
             QDC_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
             ctx->conv_smem = smem;
@@ -750,19 +733,9 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
         qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                         value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),
                         make_fastdiv(uint32_t(groups)), seq_div};
-        if (fuse) {
-            a.beta = gates.beta;
-            a.decay = gates.decay;
-            a.a_decay = gates.a_decay;
-            a.dt_bias = gates.dt_bias;
-            a.gate_start = gates.start;
-        }
         const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-        const int st = launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
-                              size_t(smem));
-        if (st != QDC_OK || fuse || gates.beta == nullptr) return st;
-        return qdc_delta_gates(ctx, gates.beta, gates.decay, proj, ld_proj, gates.start, gates.a_decay,
-                               gates.dt_bias, tokens, value_heads, stream);
+        return launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
+                      size_t(smem));
     }
     constexpr int R = 8;  // tokens per warp-unit on the register path
     const int64_t runs = (tokens + R - 1) / R;
@@ -771,20 +744,15 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
     qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                     value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)),
                     uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div};
-    int st;
     if (vec) {
         auto k = qdc::delta_conv_norm_vec<R>;
         const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32,
                                   runs * per_tok);
-        st = launch(ctx, k, grid, a, stream, "delta_conv_norm");
-    } else {
-        auto k = qdc::delta_conv_norm_generic;
-        const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
-        st = launch(ctx, k, grid, a, stream, "delta_conv_norm");
+        return launch(ctx, k, grid, a, stream, "delta_conv_norm");
     }
-    if (st != QDC_OK || gates.beta == nullptr) return st;
-    return qdc_delta_gates(ctx, gates.beta, gates.decay, proj, ld_proj, gates.start, gates.a_decay, gates.dt_bias,
-                           tokens, value_heads, stream);
+    auto k = qdc::delta_conv_norm_generic;
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
+    return launch(ctx, k, grid, a, stream, "delta_conv_norm");
 }
 
 int conv_checks(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj, int64_t ld_proj,
@@ -816,37 +784,7 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
         return s;
     if (tokens == 0) return QDC_OK;
     return conv_impl(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads, key_dim,
-                     value_heads, value_dim, eps, GateOut{}, stream);
-}
-
-int qdc_delta_prologue(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, float* beta, float* decay,
-                       const float* proj, int64_t ld_proj, const float* conv_w, int64_t gate_start,
-                       const float* a_decay, const float* dt_bias, int64_t tokens, int64_t seq_len,
-                       int key_heads, int key_dim, int value_heads, int value_dim, float eps, void* stream) {
-    if (int s = check_ctx(ctx)) return s;
-    if (int s = conv_checks(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads,
-                            key_dim, value_heads, value_dim))
-        return s;
-    const int64_t channels = 2 * int64_t(key_heads) * key_dim + int64_t(value_heads) * value_dim;
-    if (gate_start < 0 || ld_proj < gate_start + 2 * int64_t(value_heads))
-        return fail(ctx, QDC_EINVAL, "gate columns [%lld, %lld) fall outside ld_proj %lld",
-                    (long long)gate_start, (long long)(gate_start + 2 * int64_t(value_heads)), (long long)ld_proj);
-    if (gate_start < channels)
-        return fail(ctx, QDC_EINVAL, "gate columns start at %lld, inside the %lld conv channels",
-                    (long long)gate_start, (long long)channels);
-    if (tokens == 0) return QDC_OK;
-    if (!beta || !decay || !a_decay || !dt_bias)
-        return fail(ctx, QDC_EINVAL, "beta, decay, a_decay and dt_bias are required");
-    if (tokens * value_heads >= (int64_t(1) << 32) - (int64_t(1) << 24))
-        return fail(ctx, QDC_EINVAL, "too many (token, head) units");
-    GateOut g;
-    g.beta = beta;
-    g.decay = decay;
-    g.a_decay = a_decay;
-    g.dt_bias = dt_bias;
-    g.start = gate_start;
-    return conv_impl(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads, key_dim,
-                     value_heads, value_dim, eps, g, stream);
+                     value_heads, value_dim, eps, stream);
 }
 
 // ------------------------------------------------------- bf16 <-> Float32

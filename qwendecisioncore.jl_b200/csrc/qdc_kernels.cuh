@@ -673,14 +673,6 @@ struct ConvArgs {
     uint32_t units;      // vector path: runs * heads; generic: tokens * heads
     FastDiv heads_div;   // 2 kh + vh
     FastDiv seq_div;     // seq_len (tokens when unset)
-    // optional DeltaNet gates (pipeline kernel only; beta NULL: none):
-    // a of token t, value head h at proj[t*ld + gate_start + h], b at
-    // proj[t*ld + gate_start + vh + h]; beta, decay dense [tokens][vh]
-    float* beta = nullptr;
-    float* decay = nullptr;
-    const float* a_decay = nullptr;
-    const float* dt_bias = nullptr;
-    int64_t gate_start = 0;
 };
 
 struct ConvHead {
@@ -790,29 +782,13 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 constexpr int kConvPipeThreads = 768;
 
-// softplus(x) = max(x, 0) + log1p(exp(-|x|)) (src/backbone.jl:198) with the
-// library's expf / log1pf (a few ulp).
-__device__ __forceinline__ float softplus(float x) {
-    return __fadd_rn(fmaxf(x, 0.0f), log1pf(expf(-fabsf(x))));
-}
-
-// beta = inv(1 + exp(-b)) and decay = a_decay * softplus(a + dt_bias) of one
-// (token, value head), src/backbone.jl:292-297.
-__device__ __forceinline__ void delta_gate(float a, float b, float a_decay, float dt_bias, float* beta,
-                                           float* decay) {
-    *beta = __frcp_rn(__fadd_rn(1.0f, expf(-b)));
-    *decay = __fmul_rn(a_decay, softplus(__fadd_rn(a, dt_bias)));
-}
-
 template <int R, int STAGES>
 __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(ConvArgs a) {
     pdl_enter();
     constexpr int CH = 512, ROWS = R + 3, TG = kConvPipeThreads / 32 / 4, TPW = R / TG;
     static_assert(R % TG == 0 && kConvPipeThreads % (CH / 4) == 0, "tile shape");
-    extern __shared__ __align__(16) float stage_buf[];  // [STAGES][ROWS][CH], then gates [STAGES][R][2 vh]
+    extern __shared__ __align__(16) float stage_buf[];  // [STAGES][ROWS][CH]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int gate_w = a.beta ? 2 * a.vh : 0;
-    float* gate_buf = stage_buf + STAGES * ROWS * CH;
     const uint32_t groups = uint32_t(2 * a.kh + a.vh) / 4;
     const uint32_t tiles = a.units;  // runs * groups
     auto issue = [&](uint32_t tile, int stage) {
@@ -830,17 +806,6 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         for (int row = row1; row < ROWS; row += ROW_STEP, s_row += s_step) {
             const int64_t t = t0 + row;
             if (t >= 0 && t < a.tokens) cp_async16(dst + row * CH + col, s_row);
-        }
-        // the run's gate columns (a | b, 2 vh floats per token) ride with its
-        // first head group's tile
-        if (gate_w > 0 && g == 0) {
-            const int per_tok = gate_w / 4;  // 16-byte chunks per token
-            float* gdst = gate_buf + stage * (R * gate_w);
-            for (int i = tid; i < R * per_tok; i += kConvPipeThreads) {
-                const int r = i / per_tok, q4 = i - r * per_tok;
-                const int64_t t = int64_t(run) * R + r;
-                if (t < a.tokens) cp_async16(gdst + r * gate_w + q4 * 4, a.proj + t * a.ld + a.gate_start + q4 * 4);
-            }
         }
     };
 #pragma unroll
@@ -860,18 +825,6 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         const uint32_t g = tile - run * groups;
         cp_async_wait<STAGES - 1>();  // this tile's copies have landed
         __syncthreads();
-        if (gate_w > 0 && g == 0) {
-            // beta / decay of the run's tokens, consecutive threads on
-            // consecutive (token, head) outputs
-            const float* gb = gate_buf + stage * (R * gate_w);
-            for (int i = tid; i < R * a.vh; i += kConvPipeThreads) {
-                const int r = i / a.vh, hv = i - r * a.vh;
-                const int64_t t = int64_t(run) * R + r;
-                if (t < a.tokens)
-                    delta_gate(gb[r * gate_w + hv], gb[r * gate_w + a.vh + hv], __ldg(a.a_decay + hv),
-                               __ldg(a.dt_bias + hv), a.beta + t * a.vh + hv, a.decay + t * a.vh + hv);
-            }
-        }
         const ConvHead h = conv_head(a, int(g * 4 + hq));
         const int64_t c = h.c0 + lane * 4;
         float4 wt[4];  // taps 0..3 of channels c..c+3
@@ -1098,6 +1051,20 @@ struct DeltaGateArgs {
     int heads;
     FastDiv heads_div;
 };
+
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)) (src/backbone.jl:198) with the
+// library's expf / log1pf (a few ulp).
+__device__ __forceinline__ float softplus(float x) {
+    return __fadd_rn(fmaxf(x, 0.0f), log1pf(expf(-fabsf(x))));
+}
+
+// beta = inv(1 + exp(-b)) and decay = a_decay * softplus(a + dt_bias) of one
+// (token, value head), src/backbone.jl:292-297.
+__device__ __forceinline__ void delta_gate(float a, float b, float a_decay, float dt_bias, float* beta,
+                                           float* decay) {
+    *beta = __frcp_rn(__fadd_rn(1.0f, expf(-b)));
+    *decay = __fmul_rn(a_decay, softplus(__fadd_rn(a, dt_bias)));
+}
 
 // One thread per (token, head): consecutive threads read consecutive
 // columns of a token's a / b group and write consecutive outputs.

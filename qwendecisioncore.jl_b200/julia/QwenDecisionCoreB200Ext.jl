@@ -241,27 +241,6 @@ function delta_conv_norm!(query::CUDA.CuArray{Float32,3}, key::CUDA.CuArray{Floa
     return query, key, value
 end
 
-"""delta_prologue!(query, key, value, beta, decay, projected, conv, a_decay, dt_bias, cfg;
-gate_offset, seq_len)  -- delta_conv_norm! and delta_gates! in one call (one
-kernel where the shared-memory pipeline applies): the prologue of
-delta_attention (ext/cuda_delta.jl:199-216)."""
-function delta_prologue!(query::CUDA.CuArray{Float32,3}, key::CUDA.CuArray{Float32,3},
-                         value::CUDA.CuArray{Float32,3}, beta::CUDA.CuMatrix{Float32},
-                         decay::CUDA.CuMatrix{Float32}, projected::CUDA.CuMatrix{Float32}, conv, a_decay,
-                         dt_bias, cfg; gate_offset::Integer, seq_len::Integer = 0)
-    tokens = size(projected, 2)
-    ctx = context()
-    check(ccall((:qdc_delta_prologue, LIB), Cint,
-                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid},
-                 Int64, Ptr{Cvoid}, Int64, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Int64, Cint, Cint, Cint, Cint,
-                 Cfloat, Ptr{Cvoid}),
-                ctx.handle, ptr(query), ptr(key), ptr(value), ptr(beta), ptr(decay), ptr(projected),
-                Int64(size(projected, 1)), ptr(conv), Int64(gate_offset), ptr(a_decay), ptr(dt_bias),
-                Int64(tokens), Int64(seq_len), Cint(cfg.key_heads), Cint(cfg.key_dim),
-                Cint(cfg.value_heads), Cint(cfg.value_dim), 1.0f-6, stream_handle()), ctx.handle)
-    return query, key, value, beta, decay
-end
-
 """delta_solve!(system, rhs)  -- rhs .= UnitLowerTriangular(system) \\ rhs in place
 for one (n, n) system (n <= 64) or a batch (n, n, batch) / (width, n, batch)
 -- the delta_solve hook of the chunked gated delta rule (src/backbone.jl:279,
@@ -434,8 +413,7 @@ function __init__()
                                                           qk_norm_rope!,
                                                           q_k_norm_rope!, rope_tables, gated_rms!,
                                                           swiglu!, attn_gate!, delta_gates!,
-                                                          delta_conv_norm!, delta_prologue!,
-                                                          delta_solve!,
+                                                          delta_conv_norm!, delta_solve!,
                                                           upload_bf16, to_bf16!,
                                                           set_pdl!, ws_reserve!, ws_reset!,
                                                           ws_mark, ws_release!, ws_stats,

@@ -10,7 +10,7 @@ sys.path:  `import qdc_b200`.
 from ._lib import (ArgumentError, DimensionMismatch, QdcError, QDC_BF16, QDC_F32,
                    declared_symbols, load)
 from .ops import (Context, context, native_attn_gate, native_bf16_to_f32, native_delta_conv_norm,
-                  native_delta_gates, native_delta_prologue, native_delta_solve, native_f32_to_bf16,
+                  native_delta_gates, native_delta_solve, native_f32_to_bf16,
                   native_gated_rms, native_gather, native_gather_rms, native_mlp_gate,
                   native_q_k_norm_rope, native_qk_norm_rope, native_residual_add_rms,
                   native_residual_rms, native_rms, rope_table)
@@ -24,7 +24,7 @@ __all__ = [
     "check_sequence", "Config",
     "ArgumentError", "DimensionMismatch", "QdcError", "QDC_BF16", "QDC_F32", "Context", "context",
     "declared_symbols", "load", "native_attn_gate", "native_bf16_to_f32", "native_delta_conv_norm",
-    "native_delta_gates", "native_delta_prologue", "native_delta_solve", "native_f32_to_bf16",
+    "native_delta_gates", "native_delta_solve", "native_f32_to_bf16",
     "native_gated_rms", "native_gather", "native_gather_rms", "native_mlp_gate",
     "native_q_k_norm_rope", "native_qk_norm_rope", "native_residual_add_rms",
     "native_residual_rms", "native_rms", "rope_table",

@@ -80,8 +80,6 @@ SIGNATURES = {
     "qdc_delta_gates": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _vp],
     "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
                             _flt, _vp],
-    "qdc_delta_prologue": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _int,
-                           _int, _int, _int, _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],
     "qdc_unit_lower_solve": [_vp, _vp, _vp, _i64, _int, _i64, _i64, _i64, _i64, _i64, _vp],
 }

@@ -19,9 +19,8 @@ Per layer (native_layer, src/backbone.jl:363-382):
                   causal GQA attention (batched GEMMs and a softmax over
                   materialised scores, as ext/cuda_attention.jl:163-175), qdc
                   sigmoid gate read from the attention output in place, o GEMM;
-                  delta: one [qkv;z;a;b] GEMM, one qdc pass for the causal
-                  4-tap conv + SiLU + q/k L2 norms and the beta/decay gates,
-                  chunked gated delta
+                  delta: one [qkv;z;a;b] GEMM, qdc causal 4-tap conv + SiLU +
+                  q/k L2 norms, qdc beta/decay gates, chunked gated delta
                   rule (torch GEMMs + the qdc unit-lower-triangular solve),
                   qdc gated norm reading z in place, out GEMM
   post norm    -- qdc residual add + RMSNorm
@@ -344,15 +343,17 @@ class QwenBackbone:
         # masked tokens enter the DeltaNet as zeros (src/backbone.jl:286)
         masked = y if masks["maskf"] is None else torch.mul(y, masks["maskf"].view(T, 1), out=s["masked"])
         proj = torch.mm(masked, layer["proj"].t(), out=s["proj"])  # [qkv | z | a | b] per token
-        # one qdc pass over the projection: causal 4-tap conv + SiLU + q/k L2
-        # norms (src/backbone.jl:287-314), and beta = sigmoid(b), decay =
-        # a_decay * softplus(a + dt_bias) with a and b read in place
-        # (src/backbone.jl:292-297)
-        q, k, v, beta, decay = ops.native_delta_prologue(
-            proj, layer["conv"], C + vw, layer["a_decay"], layer["dt_bias"], cfg.key_heads, cfg.key_dim,
-            cfg.value_heads, cfg.value_dim, seq_len=S, q_out=s["q"], k_out=s["k"], v_out=s["v"],
-            beta=s["beta"], decay=s["decay"], ctx=self.ctx)
+        # causal 4-tap conv + SiLU + q/k L2 norms in one qdc pass over the
+        # projection (src/backbone.jl:287-314)
+        q, k, v = ops.native_delta_conv_norm(proj, layer["conv"], cfg.key_heads, cfg.key_dim,
+                                             cfg.value_heads, cfg.value_dim, seq_len=S, q_out=s["q"],
+                                             k_out=s["k"], v_out=s["v"], ctx=self.ctx)
         self._record("delta_conv_norm", (proj[:, :C], layer["conv"]), (q, k, v))
+        # beta = sigmoid(b), decay = a_decay * softplus(a + dt_bias), a and b
+        # read in place from the projection (src/backbone.jl:292-297)
+        beta, decay = ops.native_delta_gates(proj, C + vw, cfg.value_heads, layer["a_decay"],
+                                             layer["dt_bias"], beta=s["beta"], decay=s["decay"],
+                                             ctx=self.ctx)
         self._record("delta_gates", (proj[:, C + vw:C + vw + 2 * cfg.value_heads],), (beta, decay))
         o = chunked_delta(q.view(B, S, cfg.key_heads, cfg.key_dim), k.view(B, S, cfg.key_heads, cfg.key_dim),
                           v.view(B, S, cfg.value_heads, cfg.value_dim), beta.view(B, S, cfg.value_heads),

@@ -19,7 +19,6 @@ for CuArrays and the work done by the library's sm_100a kernels:
                        src/backbone.jl:287-314, ext/cuda_delta.jl:8-40,122-146
   native_delta_gates   beta / decay of delta_attention, src/backbone.jl:292-297,
                        ext/cuda_delta.jl:168-181
-  native_delta_prologue  the two above in one call (one kernel where it can)
   native_mlp_gate      src/backbone.jl:352-355, ext/cuda_mlp.jl:49-61
   native_delta_solve   delta_solve (UnitLowerTriangular(system) \\ rhs) of the
                        chunked gated delta rule, src/backbone.jl:279,
@@ -585,44 +584,6 @@ def native_delta_conv_norm(proj, conv_w, key_heads, key_dim, value_heads, value_
                                           value_heads, value_dim, float(eps), _stream(dev, stream)),
               ctx.handle)
     return q_out, k_out, v_out
-
-
-def native_delta_prologue(proj, conv_w, gate_start, a_decay, dt_bias, key_heads, key_dim, value_heads,
-                          value_dim, *, seq_len=None, eps=1e-6, q_out=None, k_out=None, v_out=None,
-                          beta=None, decay=None, ctx=None, stream=None):
-    """native_delta_conv_norm and native_delta_gates in one call (one
-    kernel where the shared-memory pipeline applies): the DeltaNet's row
-    work between its projection GEMM and the delta rule (src/backbone.jl:
-    287-297).  Returns q, k, v, beta, decay."""
-    dev = _cuda(proj, conv_w, a_decay, dt_bias, q_out, k_out, v_out, beta, decay)
-    tokens, width, ld = _rows(proj, "proj")
-    C = 2 * key_heads * key_dim + value_heads * value_dim
-    if width < C or gate_start < C or gate_start + 2 * value_heads > width:
-        raise DimensionMismatch(_lib.QDC_EINVAL, "conv channels or gate columns fall outside proj")
-    if proj.dtype != torch.float32 or conv_w.dtype != torch.float32:
-        raise ArgumentError(_lib.QDC_EINVAL, "DeltaNet prologue takes Float32 tensors")
-    w = conv_w.reshape(conv_w.shape[0], conv_w.shape[-1]).contiguous()
-    if tuple(w.shape) != (C, 4):
-        raise DimensionMismatch(_lib.QDC_EINVAL, f"conv weight must be ({C}, 4), got {tuple(conv_w.shape)}")
-    for t, name in ((a_decay, "a_decay"), (dt_bias, "dt_bias")):
-        if t.dtype != torch.float32 or t.numel() != value_heads or (value_heads > 1 and t.stride(-1) != 1):
-            raise DimensionMismatch(_lib.QDC_EINVAL, f"{name} must be {value_heads} contiguous Float32 values")
-    f = dict(dtype=torch.float32, device=dev)
-    outs = []
-    for t, shape in ((q_out, (tokens, key_heads, key_dim)), (k_out, (tokens, key_heads, key_dim)),
-                     (v_out, (tokens, value_heads, value_dim)), (beta, (tokens, value_heads)),
-                     (decay, (tokens, value_heads))):
-        t = torch.empty(shape, **f) if t is None else t
-        if tuple(t.shape) != shape or not t.is_contiguous() or t.dtype != torch.float32:
-            raise DimensionMismatch(_lib.QDC_EINVAL, "output shape differs")
-        outs.append(t)
-    ctx = ctx or context(dev)
-    with ctx.lock:
-        check(ctx.lib.qdc_delta_prologue(ctx.handle, *(_ptr(t) for t in outs), _ptr(proj), ld, _ptr(w),
-                                         int(gate_start), _ptr(a_decay), _ptr(dt_bias), tokens,
-                                         int(seq_len or 0), key_heads, key_dim, value_heads, value_dim,
-                                         float(eps), _stream(dev, stream)), ctx.handle)
-    return tuple(outs)
 
 
 def native_mlp_gate(gate, up, *, want_f32=True, want_bf16=False, out_f32=None, out_bf16=None,

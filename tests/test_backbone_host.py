@@ -119,12 +119,6 @@ def cpu_backbone(monkeypatch, oracle):
         b, d = oracle.delta_gates(c(n(proj)), start, heads, n(a_decay), n(dt_bias))
         return _put(beta, b), _put(decay, d)
 
-    def prologue(proj, w, start, a_decay, dt_bias, kh, kd, vh, vd, seq_len=None, ctx=None, q_out=None,
-                 k_out=None, v_out=None, beta=None, decay=None, **k):
-        q, kk, v = conv_norm(proj, w, kh, kd, vh, vd, seq_len=seq_len, q_out=q_out, k_out=k_out, v_out=v_out)
-        b, d = delta_gates(proj, start, vh, a_decay, dt_bias, beta=beta, decay=decay)
-        return q, kk, v, b, d
-
     def attn_gate(values, gate, ctx=None, out=None, **k):
         return _put(out, oracle.attn_gate(c(n(values)), c(n(gate))))
 
@@ -140,7 +134,6 @@ def cpu_backbone(monkeypatch, oracle):
                      ("native_qk_norm_rope", qk),
                      ("native_gated_rms", gated), ("native_mlp_gate", swiglu),
                      ("native_delta_conv_norm", conv_norm), ("native_delta_gates", delta_gates),
-                     ("native_delta_prologue", prologue),
                      ("native_attn_gate", attn_gate), ("native_delta_solve", delta_solve),
                      ("rope_table", rope_table)):
         monkeypatch.setattr(ops, name, fn)

@@ -725,50 +725,3 @@ def test_delta_solve_rejects_bad_arguments(q):
         q.native_delta_solve(torch.zeros((2, 65, 65), device="cuda"), x)
     with pytest.raises(q.DimensionMismatch):
         q.native_delta_solve(torch.zeros((2, 4, 4), device="cuda"), torch.zeros((2, 5, 8), device="cuda"))
-
-
-@pytest.mark.parametrize("tokens,seq_len,kh,kd,vh,vd,gate_pad", [
-    (4100, 2048, 16, 128, 16, 128, 0),   # the 0.8B shape: shared-memory pipeline, gates fused
-    (333, 0, 2, 128, 4, 128, 0),         # pipeline, one sequence, ragged last run
-    (200, 64, 1, 128, 2, 128, 0),        # 2*kh + vh = 4: pipeline with one head group
-    (150, 0, 2, 128, 4, 128, 1),         # gate columns not 16-byte aligned: pipeline, gates after
-    (130, 0, 1, 128, 3, 128, 0),         # 2*kh + vh = 5: register path, gates launched after
-    (97, 40, 2, 64, 4, 32, 0),           # generic path
-])
-def test_delta_prologue_equals_conv_norm_plus_gates(q, oracle, tokens, seq_len, kh, kd, vh, vd, gate_pad):
-    """qdc_delta_prologue (conv + SiLU + q/k L2 norms and the beta / decay
-    gates, one kernel where the pipeline applies) equals qdc_delta_conv_norm
-    followed by qdc_delta_gates bit for bit, and the oracle at the bar;
-    gate inputs spread over [-30, 30] reach both tails of the softplus and
-    the sigmoid."""
-    rng = np.random.default_rng(tokens + vh)
-    C = 2 * kh * kd + vh * vd
-    start = C + vh * vd + gate_pad
-    width = (start + 2 * vh + 3) // 4 * 4 + 4  # rows 16-byte aligned
-    proj = rng.standard_normal((tokens, width), dtype=np.float32)
-    proj[:, start:start + 2 * vh] = rng.uniform(-30, 30, (tokens, 2 * vh)).astype(np.float32)
-    conv = (rng.standard_normal((C, 4), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
-    a_decay = (-np.exp(rng.uniform(-1, 0.5, vh))).astype(np.float32)
-    dt_bias = rng.standard_normal(vh, dtype=np.float32)
-    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-    dproj = d(proj)
-    outs = q.native_delta_prologue(dproj, d(conv), start, d(a_decay), d(dt_bias), kh, kd, vh, vd,
-                                   seq_len=seq_len or None)
-    sep = q.native_delta_conv_norm(dproj, d(conv), kh, kd, vh, vd, seq_len=seq_len or None) + \
-        q.native_delta_gates(dproj, start, vh, d(a_decay), d(dt_bias))
-    for a, b in zip(outs, sep):
-        assert torch.equal(a, b)
-    eq, ek, ev = oracle.delta_conv_norm(proj, conv, kh, kd, vh, vd, seq_len=seq_len or None)
-    eb, ed = oracle.delta_gates(proj, start, vh, a_decay, dt_bias)
-    for a, e in zip(outs, (eq, ek, ev, eb, ed)):
-        assert f32_close(a, e)
-
-
-def test_delta_prologue_rejects_bad_gate_columns(q):
-    proj = torch.zeros((8, 2 * 128 + 2 * 128 + 2 * 2), device="cuda")
-    conv = torch.zeros((2 * 128 + 2 * 128, 4), device="cuda")
-    ab = torch.zeros(2, device="cuda")
-    with pytest.raises(q.DimensionMismatch):  # gates inside the conv channels
-        q.native_delta_prologue(proj, conv, 100, ab, ab, 1, 128, 2, 128)
-    with pytest.raises(q.DimensionMismatch):  # past the row
-        q.native_delta_prologue(proj, conv, proj.shape[1] - 3, ab, ab, 1, 128, 2, 128)

@@ -211,6 +211,20 @@ QDC_API int qdc_qk_norm_rope(qdc_ctx *ctx, float *out, const float *in,
                      int64_t table_rows, int64_t pos_offset, int64_t seq_len,
                      void *stream);
 
+/* qdc_qk_norm_rope with the output laid out by strides: head h of token t
+ * goes to out + t*out_tok + h*out_head (out_tok = heads*dim, out_head = dim
+ * is the dense layout above).  out_tok = dim, out_head = tokens*dim writes
+ * the head-major (dim, tokens, heads) Julia array that the reference's
+ * attention GEMMs read (prepare_head_kernel!, ext/cuda_attention.jl:1-45,
+ * 128,141); the heads must not overlap. */
+QDC_API int qdc_qk_norm_rope_strided(qdc_ctx *ctx, float *out, const float *in,
+                                     int64_t tokens, int heads, int dim, int64_t in_tok,
+                                     int64_t in_head, int64_t out_tok, int64_t out_head,
+                                     const float *gamma, float eps, int rotary,
+                                     const float *cos_tab, const float *sin_tab,
+                                     int64_t table_rows, int64_t pos_offset,
+                                     int64_t seq_len, void *stream);
+
 /* qdc_qk_norm_rope for the query AND key heads of the same tokens in one
  * launch: q head h of token t at q_in + t*q_tok + h*q_head, k head h at
  * k_in + t*k_tok + h*k_head; outputs dense [tokens][q_heads][dim] and
@@ -282,6 +296,18 @@ QDC_API int qdc_delta_conv_norm(qdc_ctx *ctx, float *q_out, float *k_out,
                                 int64_t tokens, int64_t seq_len, int key_heads,
                                 int key_dim, int value_heads, int value_dim,
                                 float eps, void *stream);
+
+/* qdc_delta_conv_norm with v written at v_out + t*v_tok + h*value_dim
+ * (v_tok >= value_heads*value_dim): v can go straight into the value rows of
+ * the conv output `mixed` that the reference's delta-rule kernels read
+ * (v_out = mixed + 2*key_heads*key_dim, v_tok = the qkv width;
+ * ext/cuda_delta.jl:199-213). */
+QDC_API int qdc_delta_conv_norm_strided(qdc_ctx *ctx, float *q_out, float *k_out,
+                                        float *v_out, int64_t v_tok, const float *proj,
+                                        int64_t ld_proj, const float *conv_w,
+                                        int64_t tokens, int64_t seq_len, int key_heads,
+                                        int key_dim, int value_heads, int value_dim,
+                                        float eps, void *stream);
 
 /* bf16 storage <-> Float32 on the device, n elements, out and in not
  * overlapping.  qdc_bf16_to_f32: out = bits << 16 (src/safetensors.jl:28-30),

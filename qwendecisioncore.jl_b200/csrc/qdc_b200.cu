@@ -547,11 +547,16 @@ namespace {
 
 // q/k norm + RoPE of one head group (k_heads == 0) or of the query and key
 // groups of the same tokens in one launch.
+// Output head h of token t of a group at out + t*out_tok + h*out_head.
+struct HeadOut {
+    int64_t q_tok, q_head, k_tok, k_head;
+};
+
 int qk_impl(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const float* k_in,
             int64_t tokens, int q_heads, int k_heads, int dim, int64_t q_tok, int64_t q_head,
             int64_t k_tok, int64_t k_head, const float* q_gamma, const float* k_gamma, float eps,
             int rotary, const float* cos_tab, const float* sin_tab, int64_t table_rows,
-            int64_t pos_offset, int64_t seq_len, void* stream) {
+            int64_t pos_offset, int64_t seq_len, const HeadOut& o, void* stream) {
     if (int s = check_ctx(ctx)) return s;
     if (tokens < 0 || q_heads < 1 || k_heads < 0 || dim < 1 || dim > 8192)
         return fail(ctx, QDC_EINVAL, "bad sizes tokens=%lld heads=%d+%d dim=%d", (long long)tokens,
@@ -563,7 +568,9 @@ int qk_impl(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const f
         return fail(ctx, QDC_EINVAL, "out, in and gamma are required");
     if (k_heads > 0 && (k_out == nullptr || k_in == nullptr || k_gamma == nullptr))
         return fail(ctx, QDC_EINVAL, "k_out, k_in and k_gamma are required");
-    if (q_tok < 0 || q_head < 0 || k_tok < 0 || k_head < 0) return fail(ctx, QDC_EINVAL, "negative stride");
+    if (q_tok < 0 || q_head < 0 || k_tok < 0 || k_head < 0 || o.q_tok < 0 || o.q_head < 0 || o.k_tok < 0 ||
+        o.k_head < 0)
+        return fail(ctx, QDC_EINVAL, "negative stride");
     if (pos_offset < 0) return fail(ctx, QDC_EINVAL, "negative position offset");
     if (rotary > 0) {
         if (cos_tab == nullptr || sin_tab == nullptr) return fail(ctx, QDC_EINVAL, "RoPE tables are NULL");
@@ -575,18 +582,21 @@ int qk_impl(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const f
     const int half = rotary / 2;
     const int64_t units = tokens * (q_heads + k_heads);
     bool vec = aligned16(q_out) && aligned16(q_in) && q_tok % 4 == 0 && q_head % 4 == 0 &&
-               aligned16(q_gamma) &&
+               aligned16(q_gamma) && o.q_tok % 4 == 0 && o.q_head % 4 == 0 &&
                (k_heads == 0 || (aligned16(k_out) && aligned16(k_in) && k_tok % 4 == 0 &&
-                                 k_head % 4 == 0 && aligned16(k_gamma))) &&
+                                 k_head % 4 == 0 && aligned16(k_gamma) && o.k_tok % 4 == 0 &&
+                                 o.k_head % 4 == 0)) &&
                (rotary == 0 || (half % 4 == 0 && aligned16(cos_tab) && aligned16(sin_tab)));
     // The vector kernel counts units and positions in 32 bits.
     vec = vec && units < (int64_t(1) << 32) - (int64_t(1) << 24);
     const int64_t period = seq_len > 0 ? seq_len : tokens;
     qdc::HeadArgs a{q_out, k_out, q_in, k_in, nullptr, q_gamma, k_gamma, cos_tab, sin_tab, eps,
                     q_heads, k_heads, dim, rotary, units, q_tok, q_head, k_tok, k_head, 0, 0,
-                    int64_t(q_heads) * dim, int64_t(k_heads) * dim, pos_offset, seq_len,
+                    o.q_tok, o.k_tok, pos_offset, seq_len,
                     make_fastdiv(uint32_t(q_heads + k_heads)),
                     make_fastdiv(uint32_t(period < (int64_t(1) << 31) ? period : (int64_t(1) << 31)))};
+    a.out_head = o.q_head;
+    a.out2_head = o.k_head;
     return launch_heads<false>(ctx, a, vec, stream, "qk_norm_rope");
 }
 
@@ -598,8 +608,19 @@ int qdc_qk_norm_rope(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, 
                      int64_t in_tok, int64_t in_head, const float* gamma, float eps, int rotary,
                      const float* cos_tab, const float* sin_tab, int64_t table_rows, int64_t pos_offset,
                      int64_t seq_len, void* stream) {
+    const HeadOut o{int64_t(heads) * dim, dim, 0, dim};
     return qk_impl(ctx, out, nullptr, in, nullptr, tokens, heads, 0, dim, in_tok, in_head, 0, 0, gamma,
-                   nullptr, eps, rotary, cos_tab, sin_tab, table_rows, pos_offset, seq_len, stream);
+                   nullptr, eps, rotary, cos_tab, sin_tab, table_rows, pos_offset, seq_len, o, stream);
+}
+
+int qdc_qk_norm_rope_strided(qdc_ctx* ctx, float* out, const float* in, int64_t tokens, int heads, int dim,
+                             int64_t in_tok, int64_t in_head, int64_t out_tok, int64_t out_head,
+                             const float* gamma, float eps, int rotary, const float* cos_tab,
+                             const float* sin_tab, int64_t table_rows, int64_t pos_offset, int64_t seq_len,
+                             void* stream) {
+    const HeadOut o{out_tok, out_head, 0, dim};
+    return qk_impl(ctx, out, nullptr, in, nullptr, tokens, heads, 0, dim, in_tok, in_head, 0, 0, gamma,
+                   nullptr, eps, rotary, cos_tab, sin_tab, table_rows, pos_offset, seq_len, o, stream);
 }
 
 int qdc_q_k_norm_rope(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_in, const float* k_in,
@@ -608,9 +629,10 @@ int qdc_q_k_norm_rope(qdc_ctx* ctx, float* q_out, float* k_out, const float* q_i
                       float eps, int rotary, const float* cos_tab, const float* sin_tab,
                       int64_t table_rows, int64_t pos_offset, int64_t seq_len, void* stream) {
     if (k_heads < 1) return fail(ctx, QDC_EINVAL, "k_heads must be >= 1");
+    const HeadOut o{int64_t(q_heads) * dim, dim, int64_t(k_heads) * dim, dim};
     return qk_impl(ctx, q_out, k_out, q_in, k_in, tokens, q_heads, k_heads, dim, q_tok, q_head, k_tok,
                    k_head, q_gamma, k_gamma, eps, rotary, cos_tab, sin_tab, table_rows, pos_offset,
-                   seq_len, stream);
+                   seq_len, o, stream);
 }
 
 int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int64_t rows, int heads,
@@ -631,6 +653,7 @@ int qdc_gated_rms(qdc_ctx* ctx, float* out, const float* o, const float* z, int6
     qdc::HeadArgs a{out, nullptr, o, nullptr, z, gamma, nullptr, nullptr, nullptr, eps, heads, 0, dim,
                     0, rows * heads, o_ld, dim, 0, 0, z_ld, z_off, out_ld, 0, 0, 0,
                     make_fastdiv(uint32_t(heads)), make_fastdiv(1)};
+    a.out_head = dim;
     return launch_heads<true>(ctx, a, vec, stream, "gated_rms");
 }
 
@@ -706,8 +729,8 @@ namespace {
 
 // Conv + SiLU + q/k L2 norms: the shared-memory pipeline when it applies,
 // else the register or scalar kernel.  Arguments are validated by the caller.
-int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const float* proj, int64_t ld_proj,
-              const float* conv_w, int64_t tokens, int64_t seq_len, int key_heads, int key_dim,
+int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, int64_t v_tok, const float* proj,
+              int64_t ld_proj, const float* conv_w, int64_t tokens, int64_t seq_len, int key_heads, int key_dim,
               int value_heads, int value_dim, float eps, void* stream) {
     const int64_t per_tok = 2 * int64_t(key_heads) + value_heads;
     DeviceGuard guard(ctx->device);
@@ -716,7 +739,8 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
     const qdc::FastDiv seq_div =
         make_fastdiv(uint32_t(period < (int64_t(1) << 31) ? period : (int64_t(1) << 31)));
     const bool aligned = aligned16(proj) && ld_proj % 4 == 0 && aligned16(conv_w) && aligned16(q_out) &&
-                         aligned16(k_out) && aligned16(v_out) && tokens < (int64_t(1) << 31);
+                         aligned16(k_out) && aligned16(v_out) && v_tok % 4 == 0 &&
+                         tokens < (int64_t(1) << 31);
     // Shared-memory pipeline: 48-token x 4-head tiles, 2 stages (204 KB).
     constexpr int PR = 48, PS = 2;
     const int64_t groups = per_tok / 4;
@@ -732,7 +756,7 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
         }
         qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                         value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)), uint32_t(tiles),
-                        make_fastdiv(uint32_t(groups)), seq_div};
+                        make_fastdiv(uint32_t(groups)), seq_div, v_tok};
         const int64_t grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
         return launch(ctx, k, int(grid), a, stream, "delta_conv_norm", qdc::kConvPipeThreads,
                       size_t(smem));
@@ -743,7 +767,7 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, const floa
                      runs * per_tok < (int64_t(1) << 32) - (int64_t(1) << 24);
     qdc::ConvArgs a{q_out, k_out, v_out, proj, conv_w, ld_proj, tokens, seq_len, key_heads, key_dim,
                     value_heads, value_dim, eps, 1.0f / std::sqrt(float(key_dim)),
-                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div};
+                    uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div, v_tok};
     if (vec) {
         auto k = qdc::delta_conv_norm_vec<R>;
         const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32,
@@ -783,8 +807,24 @@ int qdc_delta_conv_norm(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, 
                             key_dim, value_heads, value_dim))
         return s;
     if (tokens == 0) return QDC_OK;
-    return conv_impl(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads, key_dim,
-                     value_heads, value_dim, eps, stream);
+    return conv_impl(ctx, q_out, k_out, v_out, int64_t(value_heads) * value_dim, proj, ld_proj, conv_w, tokens,
+                     seq_len, key_heads, key_dim, value_heads, value_dim, eps, stream);
+}
+
+int qdc_delta_conv_norm_strided(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, int64_t v_tok,
+                                const float* proj, int64_t ld_proj, const float* conv_w, int64_t tokens,
+                                int64_t seq_len, int key_heads, int key_dim, int value_heads, int value_dim,
+                                float eps, void* stream) {
+    if (int s = check_ctx(ctx)) return s;
+    if (int s = conv_checks(ctx, q_out, k_out, v_out, proj, ld_proj, conv_w, tokens, seq_len, key_heads,
+                            key_dim, value_heads, value_dim))
+        return s;
+    if (v_tok < int64_t(value_heads) * value_dim)
+        return fail(ctx, QDC_EINVAL, "v_tok %lld < value_heads*value_dim %lld", (long long)v_tok,
+                    (long long)(int64_t(value_heads) * value_dim));
+    if (tokens == 0) return QDC_OK;
+    return conv_impl(ctx, q_out, k_out, v_out, v_tok, proj, ld_proj, conv_w, tokens, seq_len, key_heads,
+                     key_dim, value_heads, value_dim, eps, stream);
 }
 
 // ------------------------------------------------------- bf16 <-> Float32

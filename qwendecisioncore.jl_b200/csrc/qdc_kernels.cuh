@@ -423,6 +423,7 @@ struct HeadArgs {
     int64_t pos_offset, seq_len;
     FastDiv heads_div;   // divisor heads + heads2; units < 2^32 on the vector path
     FastDiv seq_div;     // token -> position (divisor = tokens when seq_len <= 0)
+    int64_t out_head = 0, out2_head = 0;  // output head strides (dense rows: dim)
 };
 
 struct HeadUnit {
@@ -432,7 +433,7 @@ struct HeadUnit {
     uint32_t tok;
 };
 
-__device__ __forceinline__ HeadUnit head_unit(const HeadArgs& a, uint32_t u, int dim) {
+__device__ __forceinline__ HeadUnit head_unit(const HeadArgs& a, uint32_t u) {
     HeadUnit r;
     const uint32_t per_tok = uint32_t(a.heads + a.heads2);
     r.tok = fdiv(u, a.heads_div);
@@ -441,10 +442,10 @@ __device__ __forceinline__ HeadUnit head_unit(const HeadArgs& a, uint32_t u, int
     if (r.group) {
         const int hh = h - a.heads;
         r.src = a.in2 + int64_t(r.tok) * a.in2_tok + int64_t(hh) * a.in2_head;
-        r.dst = a.out2 + int64_t(r.tok) * a.out2_tok + int64_t(hh) * dim;
+        r.dst = a.out2 + int64_t(r.tok) * a.out2_tok + int64_t(hh) * a.out2_head;
     } else {
         r.src = a.in + int64_t(r.tok) * a.in_tok + int64_t(h) * a.in_head;
-        r.dst = a.out + int64_t(r.tok) * a.out_tok + int64_t(h) * dim;
+        r.dst = a.out + int64_t(r.tok) * a.out_tok + int64_t(h) * a.out_head;
     }
     return r;
 }
@@ -488,26 +489,26 @@ __global__ void __launch_bounds__(kThreads) head_norm_vec(HeadArgs a) {
             live[k] = u < units;
             if constexpr (UPW == 1) {
                 if (k == 0 || !live[k]) {
-                    un[k] = head_unit(a, live[k] ? u : 0u, D);
+                    un[k] = head_unit(a, live[k] ? u : 0u);
                     hcur = int((live[k] ? u : 0u) - un[k].tok * uint32_t(per_tok));
                     if constexpr (GATED)
                         zcur = a.z + int64_t(un[k].tok) * a.z_tok + a.z_off + int64_t(hcur) * a.in_head;
                 } else {
                     ++hcur;
                     if (hcur == per_tok || hcur == a.heads) {
-                        un[k] = head_unit(a, u, D);
+                        un[k] = head_unit(a, u);
                         hcur = int(u - un[k].tok * uint32_t(per_tok));
                         if constexpr (GATED)
                             zcur = a.z + int64_t(un[k].tok) * a.z_tok + a.z_off + int64_t(hcur) * a.in_head;
                     } else {
                         un[k] = un[k - 1];
                         un[k].src += un[k].group ? a.in2_head : a.in_head;
-                        un[k].dst += D;
+                        un[k].dst += un[k].group ? a.out2_head : a.out_head;
                         if constexpr (GATED) zcur += a.in_head;
                     }
                 }
             } else {
-                un[k] = head_unit(a, live[k] ? u : 0u, D);
+                un[k] = head_unit(a, live[k] ? u : 0u);
             }
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c)
@@ -614,8 +615,8 @@ __global__ void __launch_bounds__(kThreads) head_norm_generic(HeadArgs a) {
         const int hh = second ? h - a.heads : h;
         const float* src = second ? a.in2 + tok * a.in2_tok + int64_t(hh) * a.in2_head
                                   : a.in + tok * a.in_tok + int64_t(hh) * a.in_head;
-        float* dst = second ? a.out2 + tok * a.out2_tok + int64_t(hh) * a.dim
-                            : a.out + tok * a.out_tok + int64_t(hh) * a.dim;
+        float* dst = second ? a.out2 + tok * a.out2_tok + int64_t(hh) * a.out2_head
+                            : a.out + tok * a.out_tok + int64_t(hh) * a.out_head;
         const float* gamma = second ? a.gamma2 : a.gamma;
         float s = 0.0f;
         for (int i = lane; i < a.dim; i += 32) {
@@ -663,7 +664,7 @@ __global__ void __launch_bounds__(kThreads) head_norm_generic(HeadArgs a) {
 struct ConvArgs {
     float* q_out;        // [tokens][kh][kd]
     float* k_out;        // [tokens][kh][kd]
-    float* v_out;        // [tokens][vh][vd]
+    float* v_out;        // token t, head h at v_out + t*v_tok + h*vd
     const float* proj;   // token rows, leading dimension ld
     const float* w;      // [channels][4]
     int64_t ld, tokens, seq_len;
@@ -673,6 +674,7 @@ struct ConvArgs {
     uint32_t units;      // vector path: runs * heads; generic: tokens * heads
     FastDiv heads_div;   // 2 kh + vh
     FastDiv seq_div;     // seq_len (tokens when unset)
+    int64_t v_tok = 0;   // token stride of v_out (dense: vh * vd)
 };
 
 struct ConvHead {
@@ -691,7 +693,7 @@ __device__ __forceinline__ ConvHead conv_head(const ConvArgs& a, int hh) {
 }
 
 __device__ __forceinline__ float* conv_dst(const ConvArgs& a, const ConvHead& h, int64_t t) {
-    if (h.group == 2) return a.v_out + (t * a.vh + h.head) * a.vd;
+    if (h.group == 2) return a.v_out + t * a.v_tok + h.head * a.vd;
     return (h.group == 0 ? a.q_out : a.k_out) + (t * a.kh + h.head) * a.kd;
 }
 
@@ -840,7 +842,7 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
         const int pos0 = int(fmod(uint32_t(t_first), a.seq_div));
         const int64_t left = a.tokens - t_first;
         const int nr = left < TPW ? int(left) : TPW;  // tokens of this warp (<= 0: none)
-        const int dst_stride = h.group == 2 ? a.vh * a.vd : a.kh * a.kd;
+        const int64_t dst_stride = h.group == 2 ? a.v_tok : int64_t(a.kh) * a.kd;
         float* dst = conv_dst(a, h, t_first) + lane * 4;
         // SiLU, the head's L2 norm for q / k, and the store of token r
         auto finish = [&](int r, float4 acc) {

@@ -137,6 +137,55 @@ function qk_norm_rope!(out::CUDA.CuArray{Float32,3}, projected::CUDA.CuMatrix{Fl
     return out
 end
 
+"""qk_norm_rope_head_major!(out, projected, weight, eps, rotary, cos, sin;
+source_width, row_offset = 0, offset = 0, groups = 1)
+
+qk_norm_rope! writing the head-major (dim, tokens, heads) layout that
+prepare_head_kernel! produces and the attention GEMMs read
+(ext/cuda_attention.jl:1-45,125-154): out[:, t, h] is head h of token t,
+source head h at rows row_offset + (h-1)*source_width .+ (1:dim) of
+column t of `projected`.  With groups > 1 the source has heads/groups heads
+and each is written to the `groups` query-head slots that read it (query
+head h reads kv head cld(h, groups)): one strided launch per slot, as the
+reference writes K once per query head.  `offset` is the position of the
+first token."""
+function qk_norm_rope_head_major!(out::CUDA.CuArray{Float32,3}, projected::CUDA.CuMatrix{Float32}, weight,
+                                  eps, rotary::Integer, cos::CUDA.CuMatrix{Float32},
+                                  sin::CUDA.CuMatrix{Float32}; source_width::Integer,
+                                  row_offset::Integer = 0, offset::Integer = 0, groups::Integer = 1)
+    dim, tokens, heads_out = size(out)
+    heads = heads_out ÷ groups
+    ctx = context()
+    for g = 0:groups-1
+        check(ccall((:qdc_qk_norm_rope_strided, LIB), Cint,
+                    (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Cint, Cint, Int64, Int64, Int64, Int64,
+                     Ptr{Cvoid}, Cfloat, Cint, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Int64, Int64, Ptr{Cvoid}),
+                    ctx.handle, ptr(out) + g * dim * tokens * sizeof(Float32),
+                    ptr(projected) + row_offset * sizeof(Float32), Int64(tokens), Cint(heads), Cint(dim),
+                    Int64(size(projected, 1)), Int64(source_width), Int64(dim),
+                    Int64(groups * dim * tokens), ptr(weight), Float32(eps), Cint(rotary), ptr(cos),
+                    ptr(sin), Int64(size(cos, 2)), Int64(offset), Int64(0), stream_handle()), ctx.handle)
+    end
+    return out
+end
+
+const ROPE_DEVICE = Dict{Tuple{Float32,Int,Int},Tuple{CUDA.CuMatrix{Float32},CUDA.CuMatrix{Float32}}}()
+const ROPE_LOCK = ReentrantLock()
+
+"""rope_device(theta, rotary, n) -> device (cos, sin) tables of at least n
+positions, built once per (theta, rotary, device) and regrown when a longer
+sequence arrives."""
+function rope_device(theta, rotary::Integer, n::Integer)
+    key = (Float32(theta), Int(rotary), CUDA.deviceid(CUDA.device()))
+    lock(ROPE_LOCK) do
+        hit = get(ROPE_DEVICE, key, nothing)
+        if hit === nothing || size(hit[1], 2) < n
+            hit = ROPE_DEVICE[key] = rope_tables(Float32(theta), rotary, max(n, 2048))
+        end
+        hit
+    end
+end
+
 """rope_tables(theta, rotary, n) -> (cos, sin) as (rotary/2, n) CuMatrices,
 built on the host exactly as src/backbone_cpu.jl:90-105."""
 function rope_tables(theta::Float32, rotary::Integer, n::Integer)
@@ -217,6 +266,27 @@ function delta_gates!(beta::CUDA.CuMatrix{Float32}, decay::CUDA.CuMatrix{Float32
                 Int64(start), ptr(a_decay), ptr(dt_bias), Int64(tokens), Cint(heads),
                 stream_handle()), ctx.handle)
     return beta, decay
+end
+
+"""delta_conv_norm_mixed!(query, key, mixed, projected, conv, cfg)  --
+delta_conv_norm! with v written into rows 2*key_width .+ (1:value_width) of
+`mixed` (qkv_width, tokens), where the reference's delta-rule kernels read
+it (ext/cuda_delta.jl:199-213); the q and k rows of `mixed` are not
+written (the delta rule reads query and key)."""
+function delta_conv_norm_mixed!(query::CUDA.CuArray{Float32,3}, key::CUDA.CuArray{Float32,3},
+                                mixed::CUDA.CuMatrix{Float32}, projected::CUDA.CuMatrix{Float32},
+                                conv::CUDA.CuMatrix{Float32}, cfg)
+    tokens = size(projected, 2)
+    key_width = cfg.key_dim * cfg.key_heads
+    ctx = context()
+    check(ccall((:qdc_delta_conv_norm_strided, LIB), Cint,
+                (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Int64, Ptr{Cvoid}, Int64, Ptr{Cvoid},
+                 Int64, Int64, Cint, Cint, Cint, Cint, Cfloat, Ptr{Cvoid}),
+                ctx.handle, ptr(query), ptr(key), ptr(mixed) + 2 * key_width * sizeof(Float32),
+                Int64(size(mixed, 1)), ptr(projected), Int64(size(projected, 1)), ptr(conv),
+                Int64(tokens), Int64(0), Cint(cfg.key_heads), Cint(cfg.key_dim), Cint(cfg.value_heads),
+                Cint(cfg.value_dim), 1.0f-6, stream_handle()), ctx.handle)
+    return query, key, mixed
 end
 
 """delta_conv_norm!(query, key, value, projected, conv, cfg)  -- the causal
@@ -410,7 +480,8 @@ function __init__()
         cuda_ext = Base.get_extension(QDC, :QwenDecisionCoreCUDAExt)
         cuda_ext === nothing || (cuda_ext.B200Kernels[] = (; residual_rms!, gather_rms!, gather!,
                                                           gather_rms_device!, gather_rms_noalloc!,
-                                                          qk_norm_rope!,
+                                                          qk_norm_rope!, qk_norm_rope_head_major!,
+                                                          rope_device, delta_conv_norm_mixed!,
                                                           q_k_norm_rope!, rope_tables, gated_rms!,
                                                           swiglu!, attn_gate!, delta_gates!,
                                                           delta_conv_norm!, delta_solve!,

@@ -70,6 +70,8 @@ SIGNATURES = {
                          _i64, _int, _vp],
     "qdc_qk_norm_rope": [_vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _vp, _flt, _int, _vp, _vp,
                          _i64, _i64, _i64, _vp],
+    "qdc_qk_norm_rope_strided": [_vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _int,
+                                 _vp, _vp, _i64, _i64, _i64, _vp],
     "qdc_q_k_norm_rope": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _i64, _i64,
                           _vp, _vp, _flt, _int, _vp, _vp, _i64, _i64, _i64, _vp],
     "qdc_gated_rms": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64, _vp, _flt, _vp],
@@ -80,6 +82,8 @@ SIGNATURES = {
     "qdc_delta_gates": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _int, _vp],
     "qdc_delta_conv_norm": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _int, _int,
                             _flt, _vp],
+    "qdc_delta_conv_norm_strided": [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _int, _int, _int,
+                                    _int, _flt, _vp],
     "qdc_swiglu": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],
     "qdc_unit_lower_solve": [_vp, _vp, _vp, _i64, _int, _i64, _i64, _i64, _i64, _i64, _vp],
 }

@@ -363,16 +363,21 @@ def native_qk_norm_rope(x, weight, eps, rotary, cos, sin, *, pos_offset=0, seq_l
         rows = cos.shape[0]
     if out is None:
         out = torch.empty((tokens, heads, dim), dtype=torch.float32, device=dev)
-    elif tuple(out.shape) != (tokens, heads, dim) or not out.is_contiguous():
-        raise DimensionMismatch(_lib.QDC_EINVAL, "output shape differs")
+    elif tuple(out.shape) != (tokens, heads, dim) or (out.numel() and dim > 1 and out.stride(2) != 1):
+        raise DimensionMismatch(_lib.QDC_EINVAL, "output must be (tokens, heads, dim) with unit inner stride")
     in_tok = x.stride(0) if tokens > 1 else heads * dim
     in_head = x.stride(1) if heads > 1 else dim
+    # any output strides (e.g. a head-major (heads, tokens, dim) buffer seen
+    # as (tokens, heads, dim)); dense outputs take the same kernel
+    out_tok = out.stride(0) if tokens > 1 else heads * dim
+    out_head = out.stride(1) if heads > 1 else dim
     ctx = ctx or context(dev)
     with ctx.lock:
-        check(ctx.lib.qdc_qk_norm_rope(
-            ctx.handle, _ptr(out), _ptr(x), tokens, heads, dim, in_tok, in_head, _ptr(weight),
-            float(eps), int(rotary), _ptr(cos) if rotary else None, _ptr(sin) if rotary else None,
-            rows, int(pos_offset), int(seq_len or 0), _stream(dev, stream)), ctx.handle)
+        check(ctx.lib.qdc_qk_norm_rope_strided(
+            ctx.handle, _ptr(out), _ptr(x), tokens, heads, dim, in_tok, in_head, out_tok, out_head,
+            _ptr(weight), float(eps), int(rotary), _ptr(cos) if rotary else None,
+            _ptr(sin) if rotary else None, rows, int(pos_offset), int(seq_len or 0), _stream(dev, stream)),
+            ctx.handle)
     return out
 
 
@@ -573,16 +578,21 @@ def native_delta_conv_norm(proj, conv_w, key_heads, key_dim, value_heads, value_
     q_out = torch.empty((tokens, key_heads, key_dim), **f) if q_out is None else q_out
     k_out = torch.empty((tokens, key_heads, key_dim), **f) if k_out is None else k_out
     v_out = torch.empty((tokens, value_heads, value_dim), **f) if v_out is None else v_out
-    for t, shape in ((q_out, (tokens, key_heads, key_dim)), (k_out, (tokens, key_heads, key_dim)),
-                     (v_out, (tokens, value_heads, value_dim))):
+    for t, shape in ((q_out, (tokens, key_heads, key_dim)), (k_out, (tokens, key_heads, key_dim))):
         if tuple(t.shape) != shape or not t.is_contiguous():
             raise DimensionMismatch(_lib.QDC_EINVAL, "output shape differs")
+    # v may be a token-strided view (heads contiguous within a token), e.g.
+    # the value rows of a wider buffer
+    if tuple(v_out.shape) != (tokens, value_heads, value_dim) or (
+            v_out.numel() and (v_out.stride(2) != 1 or (value_heads > 1 and v_out.stride(1) != value_dim))):
+        raise DimensionMismatch(_lib.QDC_EINVAL, "v_out must be (tokens, value_heads, value_dim), heads contiguous")
+    v_tok = v_out.stride(0) if tokens > 1 else value_heads * value_dim
     ctx = ctx or context(dev)
     with ctx.lock:
-        check(ctx.lib.qdc_delta_conv_norm(ctx.handle, _ptr(q_out), _ptr(k_out), _ptr(v_out), _ptr(proj),
-                                          ld, _ptr(w), tokens, int(seq_len or 0), key_heads, key_dim,
-                                          value_heads, value_dim, float(eps), _stream(dev, stream)),
-              ctx.handle)
+        check(ctx.lib.qdc_delta_conv_norm_strided(ctx.handle, _ptr(q_out), _ptr(k_out), _ptr(v_out), v_tok,
+                                                  _ptr(proj), ld, _ptr(w), tokens, int(seq_len or 0), key_heads,
+                                                  key_dim, value_heads, value_dim, float(eps),
+                                                  _stream(dev, stream)), ctx.handle)
     return q_out, k_out, v_out
 
 

@@ -725,3 +725,59 @@ def test_delta_solve_rejects_bad_arguments(q):
         q.native_delta_solve(torch.zeros((2, 65, 65), device="cuda"), x)
     with pytest.raises(q.DimensionMismatch):
         q.native_delta_solve(torch.zeros((2, 4, 4), device="cuda"), torch.zeros((2, 5, 8), device="cuda"))
+
+
+@pytest.mark.parametrize("tokens,seq_len", [(77, None), (300, 128)])
+def test_qk_norm_rope_head_major_output(q, oracle, tokens, seq_len):
+    """Output by strides (qdc_qk_norm_rope_strided): q written head-major,
+    the (dim, tokens, heads) Julia array the reference's attention GEMMs
+    read (ext/cuda_attention.jl:125-154), and K expanded to every query
+    head by one call per group (query head h reads kv head h // groups), as
+    prepare_head_kernel! lays it out; plus an output whose head stride is
+    not a multiple of 4 (the scalar kernel).  Against the oracle."""
+    r = rng(tokens)
+    Hq, Hkv, D, R = 8, 2, 256, 64
+    G = Hq // Hkv
+    proj = r.normal(0, 1, (tokens, Hq * 2 * D + Hkv * D)).astype(np.float32)
+    gq = r.normal(0, 0.02, D).astype(np.float32)
+    gk = r.normal(0, 0.02, D).astype(np.float32)
+    cos, sin = oracle.rope_table(1e7, R, 512)
+    qg = proj[:, :Hq * 2 * D].reshape(tokens, Hq, 2 * D)
+    kr = proj[:, Hq * 2 * D:].reshape(tokens, Hkv, D)
+    eq = oracle.qk_norm_rope(np.ascontiguousarray(qg[:, :, :D]), gq, 1e-6, R, cos, sin, seq_len=seq_len)
+    ek = oracle.qk_norm_rope(np.ascontiguousarray(kr), gk, 1e-6, R, cos, sin, seq_len=seq_len)
+    dp, dc, ds = dev(proj), dev(cos), dev(sin)
+    dq = dp[:, :Hq * 2 * D].view(tokens, Hq, 2 * D)[:, :, :D]
+    dk = dp[:, Hq * 2 * D:].view(tokens, Hkv, D)
+    q_hm = nan_like((Hq, tokens, D))
+    q.native_qk_norm_rope(dq, dev(gq), 1e-6, R, dc, ds, seq_len=seq_len, out=q_hm.permute(1, 0, 2))
+    assert f32_close(q_hm.permute(1, 0, 2), eq)
+    k_exp = nan_like((Hq, tokens, D))
+    for g in range(G):
+        q.native_qk_norm_rope(dk, dev(gk), 1e-6, R, dc, ds, seq_len=seq_len, out=k_exp[g::G].permute(1, 0, 2))
+    for h in range(Hq):
+        assert f32_close(k_exp[h], ek[:, h // G])
+    padded = nan_like((tokens, Hq, D + 1))
+    q.native_qk_norm_rope(dq, dev(gq), 1e-6, R, dc, ds, seq_len=seq_len, out=padded[:, :, :D])
+    assert f32_close(padded[:, :, :D], eq)
+    assert torch.isnan(padded[:, :, D]).all()
+
+
+@pytest.mark.parametrize("tokens,seq_len,kh,kd,vh,vd", [(300, 128, 2, 128, 4, 128), (130, 0, 1, 128, 3, 128),
+                                                        (50, 25, 2, 64, 3, 96)])
+def test_delta_conv_norm_v_into_mixed_rows(q, oracle, tokens, seq_len, kh, kd, vh, vd):
+    """v written through a token stride (qdc_delta_conv_norm_strided) into the
+    value rows of a (tokens, qkv width) buffer -- the conv output `mixed`
+    the reference's delta-rule kernels read v from (ext/cuda_delta.jl:199) --
+    on the pipeline, register and scalar kernels; the other rows untouched."""
+    r = rng(tokens + vh)
+    C = 2 * kh * kd + vh * vd
+    proj = r.normal(0, 1, (tokens, C + 4)).astype(np.float32)
+    w = r.normal(0, 0.5, (C, 4)).astype(np.float32)
+    eq, ek, ev = oracle.delta_conv_norm(proj, w, kh, kd, vh, vd, seq_len=seq_len or None)
+    mixed = nan_like((tokens, C))
+    v_view = mixed[:, 2 * kh * kd:].view(tokens, vh, vd)
+    gq, gk, gv = q.native_delta_conv_norm(dev(proj), dev(w), kh, kd, vh, vd, seq_len=seq_len or None,
+                                          v_out=v_view)
+    assert f32_close(gq, eq) and f32_close(gk, ek) and f32_close(v_view, ev)
+    assert torch.isnan(mixed[:, :2 * kh * kd]).all()

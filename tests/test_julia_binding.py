@@ -88,3 +88,82 @@ def test_every_declared_entry_point_is_bound():
     bound = {c[0] for c in CALLS}
     missing = sorted(set(_header()) - bound)
     assert not missing, f"declared in include/qdc_b200.h but not bound in the Julia extension: {missing}"
+
+
+# ---- the CUDA extension's side: qwendecisioncore.jl_b200/julia/patch_cuda_ext.py
+
+def _jl_functions(src):
+    """name -> (required positional count, total positional count, keyword names)
+    for every `function name(...)` and one-line `name(...) = ...` of the binding."""
+    out = {}
+    for m in re.finditer(r"^(?:function\s+)?([A-Za-z_]\w*!?)\(", src, re.M):
+        name, i, depth = m.group(1), m.end(), 1
+        while depth:
+            depth += {"(": 1, ")": -1}.get(src[i], 0)
+            i += 1
+        rest = src[i:i + 40]
+        if not (m.group(0).startswith("function") or re.match(r"\s*=", rest)):
+            continue
+        inner = src[m.end():i - 1]
+        pos, _, kw = inner.partition(";")
+        params = _split_top(pos)
+        required = sum(1 for p in params if "=" not in p)
+        out[name] = (required, len(params), {k.split("::")[0].split("=")[0].strip() for k in _split_top(kw)})
+    return out
+
+
+def _hook_calls(text):
+    """(name, positional count, keyword names) of every B200Kernels[].name(...) call."""
+    calls = []
+    for m in re.finditer(r"B200Kernels\[\]\.(\w+!?)\(", text):
+        i, depth = m.end(), 1
+        while depth:
+            depth += {"(": 1, ")": -1}.get(text[i], 0)
+            i += 1
+        pos, _, kw = text[m.end():i - 1].partition(";")
+        calls.append((m.group(1), len(_split_top(pos)), {k.split("=")[0].strip() for k in _split_top(kw)}))
+    return calls
+
+
+def _patch_module():
+    import importlib.util
+    path = os.path.join(ROOT, "qwendecisioncore.jl_b200", "julia", "patch_cuda_ext.py")
+    spec = importlib.util.spec_from_file_location("patch_cuda_ext", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_every_hook_call_names_a_binding_function_with_its_arguments():
+    """Each call the CUDA-extension edits make through the hook table names a
+    function of the binding, with a positional argument count it accepts
+    and keywords it declares; and every such function is in the table the
+    binding's __init__ fills."""
+    src = open(JL).read()
+    defs = _jl_functions(src)
+    table = re.search(r"B200Kernels\[\] = \(;(.*?)\)\)", src, re.S).group(1)
+    exported = {n.strip() for n in table.replace("\n", " ").split(",") if n.strip()}
+    calls = [c for e in _patch_module().EDITS for c in _hook_calls(e.text)]
+    assert len(calls) >= 12
+    for name, npos, kws in calls:
+        assert name in defs, f"{name} is not defined in the binding"
+        required, total, declared = defs[name]
+        assert required <= npos <= total, f"{name}: {npos} positional arguments, takes {required}..{total}"
+        assert kws <= declared, f"{name}: keywords {kws - declared} not declared"
+        assert name in exported, f"{name} is not in the hook table"
+
+
+@pytest.mark.skipif(not os.path.isdir("/root/reference/ext"), reason="the reference tree is not present")
+def test_cuda_extension_edits_apply_to_the_reference():
+    """Every edit's anchor line is where it was recorded (checked by hash) in
+    the reference's ext/ files, and the patched files bracket each routed
+    kernel launch with an if/else on the hook table."""
+    files = _patch_module().patched("/root/reference")
+    assert set(files) == {"ext/cuda_workspace.jl", "ext/cuda_mlp.jl", "ext/cuda_delta.jl",
+                          "ext/cuda_attention.jl"}
+    for name, (old, new) in files.items():
+        added = len(new.split("\n")) - len(old.split("\n"))
+        assert added > 0
+        # every `if B200Kernels[] === nothing` opened before a launch is closed
+        opens = new.count("    if B200Kernels[] === nothing\n")
+        assert new.count("\n    else\n") >= opens

@@ -84,6 +84,19 @@ __device__ __forceinline__ void st_u2(void* p, uint2 v) {
                  : "memory");
 }
 
+// 16-byte global -> shared copies that hold no registers while in flight
+// (cp.async, L2 only), committed and waited on in groups.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+
 // ------------------------------------------------------------ bf16 storage
 // src/safetensors.jl:28-30 (decode: bits << 16) and :38-42 (encode: round to
 // nearest even by integer add, no NaN special case).
@@ -772,16 +785,6 @@ __global__ void __launch_bounds__(kThreads) delta_conv_norm_vec(ConvArgs a) {
 // tokens per warp amortise the 3 halo rows each warp reads; 24 warps with
 // 48-token tiles and 2 stages (204 KB) measured 0.85 of the HBM peak
 // against 0.74 for 16 warps with 32-token tiles and 3 stages.
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                     static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-                 "l"(gmem)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 constexpr int kConvPipeThreads = 768;
 
 template <int R, int STAGES>

@@ -104,13 +104,18 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-__device__ __forceinline__ uint32_t bf16_bits(float f) {
-    uint32_t b = __float_as_uint(f);
-    return (b + 0x00007fffu + ((b >> 16) & 1u)) >> 16;
+// The rounded word: its high 16 bits are the bf16 bits.
+__device__ __forceinline__ uint32_t bf16_rounded(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return b + 0x00007fffu + ((b >> 16) & 1u);
 }
 
+__device__ __forceinline__ uint32_t bf16_bits(float f) { return bf16_rounded(f) >> 16; }
+
+// Two bf16 in one word, lo in the low half: the high halves of the two
+// rounded words, gathered by one byte permute.
 __device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
-    return bf16_bits(lo) | (bf16_bits(hi) << 16);
+    return __byte_perm(bf16_rounded(lo), bf16_rounded(hi), 0x7632);
 }
 
 // A 16-byte chunk of a row (4 Float32 or 8 bf16 values) as loaded: the raw

@@ -230,7 +230,7 @@ class QwenBackbone:
             self._rope[self.config.rotary_dim] = hit
         return hit
 
-    def _upper(self, n, diagonal=1):
+    def _upper(self, n):
         """(n, n) bool, True strictly above the diagonal (made once per n)."""
         key = ("upper", n)
         t = self._const.get(key)

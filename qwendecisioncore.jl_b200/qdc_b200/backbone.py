@@ -55,6 +55,7 @@ from .workspace import Workspace, slot_bytes, spec_bytes
 
 FLOATMAX32 = float(np.finfo(np.float32).max)
 MAX_GRAPHS = 32  # cached last-token graphs per model (shapes beyond evict the oldest)
+MAX_CONSTS = 8  # cached causal masks per model (one per sequence length in use)
 DELTA_CHUNK = 64  # src/backbone.jl:301, ext/cuda_delta_chunked.jl:9
 SCAN_MAX_HEADS = 64  # batch x value heads up to which the delta hand-off runs as a linear scan
 ATTN_SCORE_BYTES = 1 << 30  # attention scores per chunk of sequences (one buffer)
@@ -199,7 +200,10 @@ class QwenBackbone:
 
     def _init_caches(self):
         self._rope = {}
-        self._const = {}  # device constants made once per size (causal masks)
+        # device constants made once per size (causal masks), least recently
+        # used first; at most MAX_CONSTS are kept (a captured graph holds
+        # its own references to the ones it reads)
+        self._const = collections.OrderedDict()
         # (B, S, full_mask) -> captured last-token forward, least recently
         # used first; at most MAX_GRAPHS are kept
         self._graphs = collections.OrderedDict()
@@ -235,7 +239,10 @@ class QwenBackbone:
         key = ("upper", n)
         t = self._const.get(key)
         if t is None:
+            while len(self._const) >= MAX_CONSTS:
+                self._const.popitem(last=False)
             t = self._const[key] = torch.ones((n, n), dtype=torch.bool, device=self.device).triu_(1)
+        self._const.move_to_end(key)
         return t
 
     def _record(self, site, inputs, outputs):
@@ -570,6 +577,7 @@ class _GraphedLastHidden:
             # the captured kernels read these tables by address: hold them, as
             # the model's cache replaces them when a longer sequence arrives
             self.rope = model.rope(S)
+            self.consts = tuple(model._const.values())  # the masks the capture reads
             graph = torch.cuda.CUDAGraph()
             # thread_local: CUDA calls that other host threads make meanwhile
             # (outside this model's lock) do not invalidate the capture

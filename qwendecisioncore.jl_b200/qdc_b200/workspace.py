@@ -23,6 +23,7 @@ for the same reason, src/backbone.jl:440-452)."""
 import torch
 
 GROWTH = 1.5  # a growing arena takes at least this factor more, so growth events stay few
+MAX_VIEWS = 4096  # cached slot views (a forward carves a few hundred)
 
 
 class Workspace:
@@ -61,6 +62,8 @@ class Workspace:
         key = (ptr - self._base, shape, dtype)
         view = self._views.get(key)
         if view is None:
+            if len(self._views) >= MAX_VIEWS:  # many shapes seen: start over
+                self._views.clear()
             view = self._views[key] = self.ctx.wrap(ptr, shape, dtype)
         return view
 

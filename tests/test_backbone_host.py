@@ -382,3 +382,21 @@ def test_workspace_slots_repeat_by_call_order(cpu_backbone):
     assert len(set(spans[(proj_delta, torch.float32)])) == 1 and len(spans[(proj_delta, torch.float32)]) == 3
     proj_full = (2 * 70, cfg.heads * 2 * cfg.head_dim + 2 * cfg.kv_heads * cfg.head_dim)
     assert len(set(spans[(proj_full, torch.float32)])) == 1 and len(spans[(proj_full, torch.float32)]) == 2
+
+
+def test_constant_caches_stay_bounded(cpu_backbone):
+    """A model that sees many sequence lengths keeps at most MAX_CONSTS
+    causal masks (each S x S on the device), least recently used evicted,
+    and results do not depend on what was evicted."""
+    import qdc_b200
+    from qdc_b200 import backbone as BB
+    from qdc_b200.model import load_weights
+    cfg, w = load_weights(GOLDEN)
+    model = cpu_backbone(cfg, w)
+    first = qdc_b200.backbone_hidden(model, np.arange(5) % 64, np.ones(5, np.int64))
+    for n in range(6, 6 + 2 * BB.MAX_CONSTS):
+        qdc_b200.backbone_hidden(model, np.arange(n) % 64, np.ones(n, np.int64))
+        assert len(model._const) <= BB.MAX_CONSTS
+    assert ("upper", 5) not in model._const
+    again = qdc_b200.backbone_hidden(model, np.arange(5) % 64, np.ones(5, np.int64))
+    assert np.array_equal(again, first)

@@ -80,10 +80,10 @@ assert BYTES_PER_TOKEN == 2_392_064
 
 # DRAM bytes per token of the dominant kernel (SwiGLU, fp32 out), from one
 # ncu --set full capture of `bench.py --kernel swiglu --tokens 16384`:
-# dram__bytes_read + dram__bytes_write = 651,569,664 B for 16,384 tokens.  Traffic grows in
+# dram__bytes_read + dram__bytes_write = 651,256,320 B for 16,384 tokens.  Traffic grows in
 # proportion to the tokens (a pure stream), so a full launch's traffic is
 # this times its tokens.
-SWIGLU_DRAM_BYTES_PER_TOKEN = 651_569_664 / 16384
+SWIGLU_DRAM_BYTES_PER_TOKEN = 651_256_320 / 16384
 
 
 def hbm_peak():

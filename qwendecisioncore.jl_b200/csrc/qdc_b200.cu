@@ -3,8 +3,8 @@
 // Host side of the library: context + workspace arena, argument validation
 // (every check happens before anything is launched), launch-shape selection
 // (vector kernel specialised on the row width when every operand is 16-byte
-// aligned, scalar kernel otherwise) and persistent grid sizing from the
-// occupancy calculator.
+// aligned, scalar kernel otherwise) and grid sizing from the occupancy
+// calculator and the amount of work.
 #include "qdc_b200.h"
 #include "qdc_kernels.cuh"
 
@@ -112,23 +112,32 @@ int qdc_resident_blocks(const void* kernel, int device, int threads) {
     return n;
 }
 
-// Persistent grid of at most one full wave (shared with qdc_noalloc.cu).
-// When the work takes three or more grid-stride rounds at full occupancy,
-// every resident slot is used: the extra warps keep more bytes in flight and
-// the kernel stays bandwidth-bound through a ragged last round (measured on
-// B200, chains of residual-norm launches: 6.11 TB/s and 1.9 us fixed per
-// launch, against 6.03 TB/s and 2.3 us for grids trimmed to equal rounds).
-// With one or two rounds the grid is trimmed so that every round is full
-// (4,096 rows: 12.7 us against 12.9).
+// Grid rule (shared with qdc_noalloc.cu).  Every kernel it sizes walks its
+// units in a grid-stride loop, so any grid is correct; the rule picks the
+// fastest one measured on B200.
+//  - Work of three or more rounds of a full wave: one block per
+//    `work_per_block_units` units (one unit per warp), so blocks retire and
+//    new ones start as soon as a slot frees and no warp waits on a ragged
+//    last round (chains of residual-norm launches, 1024 wide: 65,536 rows
+//    159.0 us against 174.3 us for a persistent full-wave grid; 16,384 rows
+//    42.2 against 45.0; 8,192 rows 23.1 against 23.2).  The grid stops at
+//    kMaxGrid blocks (2^16): with at most 256 threads and 16 units per warp
+//    step a grid-stride loop's stride then stays within 2^24 units, the
+//    headroom that the 32-bit unit counters' host checks leave.
+//  - One or two rounds: the grid is trimmed so that every round is full (a
+//    tiny launch spends less on block start-up: the DeltaNet gates over
+//    32,768 x 16 units take 4.0 us against 4.3 with one unit per warp).
 int64_t qdc_grid_size(int64_t cap, int64_t work_per_block_units, int64_t units) {
+    constexpr int64_t kMaxGrid = int64_t(1) << 16;
     if (units < 1) units = 1;
     if (work_per_block_units < 1) work_per_block_units = 1;
+    if (cap < 1) cap = 1;
     const int64_t per_wave = cap * work_per_block_units;
     const int64_t rounds = (units + per_wave - 1) / per_wave;
-    if (rounds >= 3) return cap;
-    const int64_t per_block = rounds * work_per_block_units;
+    const int64_t per_block = rounds >= 3 ? work_per_block_units : rounds * work_per_block_units;
     int64_t g = (units + per_block - 1) / per_block;
-    if (g > cap) g = cap;
+    if (rounds < 3 && g > cap) g = cap;
+    if (g > kMaxGrid) g = kMaxGrid;
     return g < 1 ? 1 : g;
 }
 

@@ -2,8 +2,10 @@
 //
 // All of these ops stream rows through HBM once: no dense contraction, so no
 // tensor cores.  The design that follows from that:
-//  * one warp per row (or per head segment of a row), persistent grid sized
-//    from the occupancy calculator x 148 SMs, rows handed out grid-stride;
+//  * one warp per row (or per head segment of a row), rows handed out
+//    grid-stride; the host sizes the grid to one row per warp when the work
+//    fills three or more waves (occupancy calculator x 148 SMs), else to
+//    equal full rounds;
 //  * every load of a row is issued before any arithmetic (16-byte
 //    ld.global.nc per lane, the whole row in flight), so a warp keeps
 //    4-8 KB outstanding and ~20-30 resident warps per SM cover HBM latency;
@@ -38,10 +40,9 @@ constexpr int kThreads = 256;  // 8 warps per CTA for the vector kernels
 // drains.  Each kernel first waits for the predecessor grid to complete
 // (griddepcontrol.wait -- a no-op when launched without the attribute) and
 // only then touches global memory, then lets its own successor start
-// launching.  The option is off by default: these persistent grids fill
-// every SM, so a successor's CTAs find no room until the predecessor's exit,
-// and chains of row kernels measured a 2.9 us fixed cost per launch with it
-// against 2.4 us without.
+// launching.  The option is off by default: on chains of row kernels it
+// saved 0.1-0.2 us per launch (a 1-wave grid of persistent warps measured a
+// 2.9 us fixed cost per launch with it against 2.4 us without).
 __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -126,7 +126,7 @@ extern "C" int qdc_gather_rms_noalloc(void* out_x, void* out_y, const void* tabl
                      aligned16(gamma) && (hidden * esz) % 16 == 0;
     const qdc::RowKernel k = dtype == QDC_F32 ? qdc::row_kernel_for<float>(hidden, vec)
                                               : qdc::row_kernel_for<uint16_t>(hidden, vec);
-    // persistent grid of at most one wave (the context path's rule)
+    // the context path's grid rule
     const int64_t cap = int64_t(s.sm_count) *
                         qdc_resident_blocks(reinterpret_cast<const void*>(k), device, qdc::kThreads);
     const int64_t grid = qdc_grid_size(cap, qdc::kThreads / 32, n);

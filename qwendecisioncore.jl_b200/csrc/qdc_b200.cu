@@ -21,7 +21,7 @@
 struct qdc_ctx {
     int device = -1;
     int sm_count = 0;
-    bool pdl = false;  // QDC_OPT_PDL
+    bool pdl = true;  // QDC_OPT_PDL
     int conv_smem = 0;  // DeltaNet pipeline's dynamic shared memory limit, as raised
     std::string err;
     // workspace arena
@@ -497,14 +497,17 @@ namespace {
 using HeadKernel = void (*)(qdc::HeadArgs);
 
 // Vector head kernel for `dim`, and the units (LPU lanes each) a warp takes
-// per iteration.  With very few units the grid needs more, smaller work
-// items (ramp and tail dominate); otherwise the wider unroll keeps more
-// bytes in flight.  Since a warp's consecutive units step their row
-// pointers instead of dividing per unit, the wider unroll wins from 81,920
-// units up (measured on B200: q/k +2.4% at 8,192 tokens x 10 heads, +4% at
-// 65,536; gated +0.6% at 8,192 x 16), so only small launches keep the
-// narrow one.
-constexpr int64_t kManyUnits = 32768;
+// per iteration.  The grid rule gives each warp one iteration of a large
+// launch, so the unroll sets the bytes a warp has in flight against the
+// registers it costs; fewer registers mean more resident warps.  Measured
+// on B200 with one unit per warp step against two and four: q/k (256 dims,
+// 64 registers at two units, 40 at one) 0.989 of the copy peak against
+// 0.932 at 65,536 tokens x 10 heads and 0.880 against 0.854 at 8,192; the
+// gated norm (128 dims) 0.987 against 0.970 / 0.955 at 8,192 x 16 units and
+// 1.032 against 1.023 / 1.016 at 16,384, while two units win from 2^20 units
+// up (1.066 against 1.056 at 65,536 x 16).  The 32- and 64-dim kernels keep
+// four units per step (a warp covers 4 and 2 units per step there).
+constexpr int64_t kManyUnits = int64_t(1) << 20;
 
 template <bool GATED>
 HeadKernel head_vec_kernel(int dim, int64_t units, int* lpu, int* unroll) {
@@ -514,14 +517,10 @@ HeadKernel head_vec_kernel(int dim, int64_t units, int* lpu, int* unroll) {
         case 64: *lpu = 16; *unroll = 4; return qdc::head_norm_vec<16, 1, 4, GATED>;
         case 128:
             *lpu = 32;
-            if (many) { *unroll = 4; return qdc::head_norm_vec<32, 1, 4, GATED>; }
-            *unroll = 2;
-            return qdc::head_norm_vec<32, 1, 2, GATED>;
-        case 256:
-            *lpu = 32;
-            if (many) { *unroll = 2; return qdc::head_norm_vec<32, 2, 2, GATED>; }
+            if (many) { *unroll = 2; return qdc::head_norm_vec<32, 1, 2, GATED>; }
             *unroll = 1;
-            return qdc::head_norm_vec<32, 2, 1, GATED>;
+            return qdc::head_norm_vec<32, 1, 1, GATED>;
+        case 256: *lpu = 32; *unroll = 1; return qdc::head_norm_vec<32, 2, 1, GATED>;
         case 512: *lpu = 32; *unroll = 1; return qdc::head_norm_vec<32, 4, 1, GATED>;
         default: return nullptr;
     }

@@ -427,7 +427,7 @@ function to_bf16!(out::CUDA.CuArray{UInt16}, x::CUDA.CuArray{Float32})
 end
 
 """set_pdl!(on::Bool)  -- QDC_OPT_PDL: programmatic dependent launch for this
-device's context (off by default)."""
+device's context (on by default)."""
 set_pdl!(on::Bool) = check(ccall((:qdc_set_option, LIB), Cint, (Ptr{Cvoid}, Cint, Cint),
                                  context().handle, Cint(1), Cint(on)), context().handle)
 

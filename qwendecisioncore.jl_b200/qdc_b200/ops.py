@@ -59,11 +59,11 @@ class Context:
         check(self.lib.qdc_init(self.device.index or 0, ctypes.byref(handle)))
         self.handle = handle
         self.lock = threading.RLock()
-        self._pdl = False
+        self._pdl = True
 
     @property
     def pdl(self):
-        """Programmatic dependent launch of this context's kernels (off by
+        """Programmatic dependent launch of this context's kernels (on by
         default; QDC_OPT_PDL of include/qdc_b200.h)."""
         return self._pdl
 

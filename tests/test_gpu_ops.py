@@ -472,8 +472,9 @@ def test_row_kernel_waits_for_its_producer(q, oracle, width_heads):
     ex_r, ex_y = oracle.residual_rms(gated, m, wr, 1e-6)
     do, dz, dwg, dm, dwr = dev(o), dev(z), dev(wg), dev(m), dev(wr)
     ctx = q.context(torch.device("cuda", 0))
+    before = ctx.pdl
     try:
-        ctx.pdl = True  # QDC_OPT_PDL: the launch mode in which the wait matters
+        ctx.pdl = True  # QDC_OPT_PDL (the default): the launch mode in which the wait matters
         for _ in range(3):
             g = nan_like((T, H * D))
             q.native_gated_rms(do, dz, dwg, 1e-6, out=g, ctx=ctx)
@@ -482,7 +483,7 @@ def test_row_kernel_waits_for_its_producer(q, oracle, width_heads):
             assert not torch.isnan(yy).any()
             assert f32_close(rr, ex_r) and f32_close(yy, ex_y)
     finally:
-        ctx.pdl = False
+        ctx.pdl = before
 
 
 def _misaligned(a):
@@ -609,24 +610,25 @@ def test_bf16_checkpoint_upload_matches_host_widening(q, oracle, tmp_path):
 
 
 def test_pdl_option(q, oracle):
-    """QDC_OPT_PDL on launches the same kernels with programmatic dependent
-    launch: identical results; an unknown option is refused."""
+    """QDC_OPT_PDL (on by default) launches the same kernels with
+    programmatic dependent launch: identical results with it off and on; an
+    unknown option is refused."""
     from qdc_b200 import _lib
     ctx = q.context(torch.device("cuda", 0))
-    assert not ctx.pdl
+    assert ctx.pdl
     r = rng(3)
     x = r.normal(0, 1, (300, 1024)).astype(np.float32)
     m = r.normal(0, 1, (300, 1024)).astype(np.float32)
     w = r.normal(0, 0.02, 1024).astype(np.float32)
-    off = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
     try:
-        ctx.pdl = True
-        g = nan_like((300, 1024))
-        q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, out_y=g, ctx=ctx)  # producer ...
-        on = q.native_residual_rms(g, dev(m), dev(w), 1e-6, ctx=ctx)       # ... and consumer
+        ctx.pdl = False
+        off = q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, ctx=ctx)
         ref = q.native_residual_rms(off[1], dev(m), dev(w), 1e-6, ctx=ctx)
     finally:
-        ctx.pdl = False
+        ctx.pdl = True
+    g = nan_like((300, 1024))
+    q.native_residual_rms(dev(x), dev(m), dev(w), 1e-6, out_y=g, ctx=ctx)  # producer ...
+    on = q.native_residual_rms(g, dev(m), dev(w), 1e-6, ctx=ctx)       # ... and consumer
     assert torch.equal(on[0], ref[0]) and torch.equal(on[1], ref[1])
     with pytest.raises(q.ArgumentError):
         _lib.check(ctx.lib.qdc_set_option(ctx.handle, 99, 1), ctx.handle)

@@ -121,14 +121,14 @@ int qdc_resident_blocks(const void* kernel, int device, int threads) {
 //    last round (chains of residual-norm launches, 1024 wide: 65,536 rows
 //    159.0 us against 174.3 us for a persistent full-wave grid; 16,384 rows
 //    42.2 against 45.0; 8,192 rows 23.1 against 23.2).  The grid stops at
-//    kMaxGrid blocks (2^16): with at most 256 threads and 16 units per warp
-//    step a grid-stride loop's stride then stays within 2^24 units, the
-//    headroom that the 32-bit unit counters' host checks leave.
+//    kMaxGrid = 2^24 / kThreads blocks: with 16 units per warp step at most,
+//    a grid-stride loop's stride then stays within 2^24 units, the headroom
+//    that the 32-bit unit counters' host checks leave.
 //  - One or two rounds: the grid is trimmed so that every round is full (a
 //    tiny launch spends less on block start-up: the DeltaNet gates over
 //    32,768 x 16 units take 4.0 us against 4.3 with one unit per warp).
 int64_t qdc_grid_size(int64_t cap, int64_t work_per_block_units, int64_t units) {
-    constexpr int64_t kMaxGrid = int64_t(1) << 16;
+    constexpr int64_t kMaxGrid = (int64_t(1) << 24) / qdc::kThreads;
     if (units < 1) units = 1;
     if (work_per_block_units < 1) work_per_block_units = 1;
     if (cap < 1) cap = 1;
@@ -147,10 +147,21 @@ int resident_blocks(const void* kernel, int device, int threads) {
     return qdc_resident_blocks(kernel, device, threads);
 }
 
-int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units) {
-    const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, qdc::kThreads);
+int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units,
+             int threads = qdc::kThreads) {
+    const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, threads);
     return int(qdc_grid_size(cap, work_per_block_units, units));
 }
+
+// Block size of the q/k head kernels and the BF16 conversions.  Every other
+// kernel runs blocks of qdc::kThreads (256) threads; these two measured
+// faster with 128 on B200 (q/k norm + RoPE at 16,384 tokens x 10 heads:
+// 0.961 of the copy peak against 0.936, 0.984 against 0.967 inside the
+// 65,536-token step; the BF16 -> Float32 widen of a 151,936 x 1,024 table:
+// 0.934 against 0.876), while the row, gated and SwiGLU kernels were level
+// or slower with 128 (the 24-layer step at 16,384 tokens: 6.21 ms against
+// 6.04 with every kernel at 128).
+constexpr int kSmallThreads = 128;
 
 // Launch, with programmatic stream serialization when the context turned it
 // on (QDC_OPT_PDL; see qdc_kernels.cuh).
@@ -535,14 +546,16 @@ int launch_heads(qdc_ctx* ctx, const qdc::HeadArgs& a, bool vec_ok, void* stream
     HeadKernel k = vec_ok ? head_vec_kernel<GATED>(a.dim, a.units, &lpu, &unroll) : nullptr;
     if (k != nullptr && !GATED && a.rotary > 4 * lpu) k = nullptr;  // rotary must lie in chunk 0
     int64_t units_per_block;
+    int threads = qdc::kThreads;
     if (k == nullptr) {
         k = qdc::head_norm_generic<GATED>;
-        units_per_block = qdc::kThreads / 32;
+        units_per_block = threads / 32;
     } else {
-        units_per_block = int64_t(qdc::kThreads / 32) * (32 / lpu) * unroll;
+        if (!GATED) threads = kSmallThreads;
+        units_per_block = int64_t(threads / 32) * (32 / lpu) * unroll;
     }
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), units_per_block, a.units);
-    return launch(ctx, k, grid, a, stream, name);
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), units_per_block, a.units, threads);
+    return launch(ctx, k, grid, a, stream, name, threads);
 }
 
 }  // namespace
@@ -855,9 +868,9 @@ int convert(qdc_ctx* ctx, void* out, const void* in, int64_t n, bool widen, void
     // (vector) or single elements
     int64_t items = vec ? (n / 8 + qdc::kConvertUnroll - 1) / qdc::kConvertUnroll : n;
     if (items < 1) items = 1;  // n < 8: the tail loop alone
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads, items);
+    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), kSmallThreads, items, kSmallThreads);
     qdc::ConvertArgs a{out, in, n};
-    return launch(ctx, k, grid, a, stream, widen ? "bf16_to_f32" : "f32_to_bf16");
+    return launch(ctx, k, grid, a, stream, widen ? "bf16_to_f32" : "f32_to_bf16", kSmallThreads);
 }
 }  // namespace
 

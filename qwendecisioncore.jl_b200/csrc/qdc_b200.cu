@@ -3,8 +3,8 @@
 // Host side of the library: context + workspace arena, argument validation
 // (every check happens before anything is launched), launch-shape selection
 // (vector kernel specialised on the row width when every operand is 16-byte
-// aligned, scalar kernel otherwise) and grid sizing from the occupancy
-// calculator and the amount of work.
+// aligned, scalar kernel otherwise) and grid sizing from the amount of
+// work.
 #include "qdc_b200.h"
 #include "qdc_kernels.cuh"
 
@@ -14,9 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
-#include <mutex>
 #include <string>
-#include <unordered_map>
 
 struct qdc_ctx {
     int device = -1;
@@ -92,76 +90,40 @@ struct DeviceGuard {
 
 }  // namespace
 
-// Blocks per SM that keep one instance of `kernel` resident, cached per
-// (kernel, device, block size).  Shared with qdc_noalloc.cu (not exported).
-int qdc_resident_blocks(const void* kernel, int device, int threads) {
-    static std::mutex mu;
-    static std::unordered_map<uint64_t, int> cache;
-    const uint64_t key = reinterpret_cast<uint64_t>(kernel) ^ (uint64_t(device) << 56) ^
-                         (uint64_t(threads) << 40);
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        auto it = cache.find(key);
-        if (it != cache.end()) return it->second;
-    }
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n < 1)
-        n = 1;
-    std::lock_guard<std::mutex> lock(mu);
-    cache[key] = n;
-    return n;
-}
-
-// Grid rule (shared with qdc_noalloc.cu).  Every kernel it sizes walks its
-// units in a grid-stride loop, so any grid is correct; the rule picks the
-// fastest one measured on B200.
-//  - Work of three or more rounds of a full wave: one block per
-//    `work_per_block_units` units (one unit per warp), so blocks retire and
-//    new ones start as soon as a slot frees and no warp waits on a ragged
-//    last round (chains of residual-norm launches, 1024 wide: 65,536 rows
-//    159.0 us against 174.3 us for a persistent full-wave grid; 16,384 rows
-//    42.2 against 45.0; 8,192 rows 23.1 against 23.2).  The grid stops at
-//    kMaxGrid = 2^24 / kThreads blocks: with 16 units per warp step at most,
-//    a grid-stride loop's stride then stays within 2^24 units, the headroom
-//    that the 32-bit unit counters' host checks leave.
-//  - One or two rounds: the grid is trimmed so that every round is full (a
-//    tiny launch spends less on block start-up: the DeltaNet gates over
-//    32,768 x 16 units take 4.0 us against 4.3 with one unit per warp).
-int64_t qdc_grid_size(int64_t cap, int64_t work_per_block_units, int64_t units) {
-    constexpr int64_t kMaxGrid = (int64_t(1) << 24) / qdc::kThreads;
+// Grid rule (shared with qdc_noalloc.cu): one block per
+// `work_per_block_units` units, that is one unit (a row, or a (token, head)
+// group) per warp step.  Every kernel it sizes walks its units in a
+// grid-stride loop, so any grid is correct; this one measured fastest on
+// B200.  Blocks retire and new ones start as soon as a slot frees, so no
+// warp waits on a ragged last round of a persistent grid, and the successor
+// kernel's blocks (programmatic dependent launch) fill the slots as they
+// free.  Chains of residual-norm launches, 1024 wide, against a persistent
+// full-wave grid: 65,536 rows 159.0 us against 174.3; 16,384 rows 42.2
+// against 45.0.  Against grids trimmed to equal full rounds (the earlier
+// rule for launches of one or two waves): 4,096 rows 11.0 us against 13.6,
+// SwiGLU over 8,192 x 3,584 55.5 against 59.3, the DeltaNet gates over
+// 32,768 x 16 units 3.47 against 3.69.  `work_per_block_units` counts the
+// units of the kernel's own loop counter that one block covers per step, so
+// the loop's stride is grid x work_per_block_units; the grid stops where
+// that reaches 2^24 units, the headroom that the host checks of the 32-bit
+// unit counters leave (a launch that large loops instead).
+int64_t qdc_grid_size(int64_t work_per_block_units, int64_t units) {
+    constexpr int64_t kMaxStride = int64_t(1) << 24;
     if (units < 1) units = 1;
     if (work_per_block_units < 1) work_per_block_units = 1;
-    if (cap < 1) cap = 1;
-    const int64_t per_wave = cap * work_per_block_units;
-    const int64_t rounds = (units + per_wave - 1) / per_wave;
-    const int64_t per_block = rounds >= 3 ? work_per_block_units : rounds * work_per_block_units;
-    int64_t g = (units + per_block - 1) / per_block;
-    if (rounds < 3 && g > cap) g = cap;
-    if (g > kMaxGrid) g = kMaxGrid;
+    int64_t g = (units + work_per_block_units - 1) / work_per_block_units;
+    const int64_t max_grid = kMaxStride / work_per_block_units;
+    if (g > max_grid) g = max_grid;
     return g < 1 ? 1 : g;
 }
 
 namespace {
 
-int resident_blocks(const void* kernel, int device, int threads) {
-    return qdc_resident_blocks(kernel, device, threads);
+int grid_for(int64_t work_per_block_units, int64_t units) {
+    return int(qdc_grid_size(work_per_block_units, units));
 }
 
-int grid_for(qdc_ctx* ctx, const void* kernel, int64_t work_per_block_units, int64_t units,
-             int threads = qdc::kThreads) {
-    const int64_t cap = int64_t(ctx->sm_count) * resident_blocks(kernel, ctx->device, threads);
-    return int(qdc_grid_size(cap, work_per_block_units, units));
-}
-
-// Block size of the q/k head kernels and the BF16 conversions.  Every other
-// kernel runs blocks of qdc::kThreads (256) threads; these two measured
-// faster with 128 on B200 (q/k norm + RoPE at 16,384 tokens x 10 heads:
-// 0.961 of the copy peak against 0.936, 0.984 against 0.967 inside the
-// 65,536-token step; the BF16 -> Float32 widen of a 151,936 x 1,024 table:
-// 0.934 against 0.876), while the row, gated and SwiGLU kernels were level
-// or slower with 128 (the 24-layer step at 16,384 tokens: 6.21 ms against
-// 6.04 with every kernel at 128).
-constexpr int kSmallThreads = 128;
+using qdc::kSmallThreads;
 
 // Launch, with programmatic stream serialization when the context turned it
 // on (QDC_OPT_PDL; see qdc_kernels.cuh).
@@ -198,8 +160,8 @@ int launch_rows(qdc_ctx* ctx, const qdc::RowArgs& a, void* stream) {
                (a.out_r == nullptr || (a.ld_r * e) % 16 == 0) &&
                (a.m == nullptr || (a.ld_m * e) % 16 == 0);
     const qdc::RowKernel k = qdc::row_kernel_for<T>(a.width, vec);
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, a.rows);
-    return launch(ctx, k, grid, a, stream, "row_rms");
+    const int grid = grid_for(kSmallThreads / 32, a.rows);
+    return launch(ctx, k, grid, a, stream, "row_rms", kSmallThreads);
 }
 
 int check_ctx(qdc_ctx* ctx) {
@@ -554,7 +516,7 @@ int launch_heads(qdc_ctx* ctx, const qdc::HeadArgs& a, bool vec_ok, void* stream
         if (!GATED) threads = kSmallThreads;
         units_per_block = int64_t(threads / 32) * (32 / lpu) * unroll;
     }
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), units_per_block, a.units, threads);
+    const int grid = grid_for(units_per_block, a.units);
     return launch(ctx, k, grid, a, stream, name, threads);
 }
 
@@ -710,7 +672,7 @@ int qdc_attn_gate(qdc_ctx* ctx, float* out, const float* values, const float* ga
             default: break;
         }
     }
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, units);
+    const int grid = grid_for(qdc::kThreads / 32, units);
     return launch(ctx, k, grid, a, stream, "attn_gate");
 }
 
@@ -736,9 +698,8 @@ int qdc_delta_gates(qdc_ctx* ctx, float* beta, float* decay, const float* proj, 
     if (guard.status != cudaSuccess) return cuda_fail(ctx, guard.status, "cudaSetDevice");
     qdc::DeltaGateArgs a{beta, decay, proj, a_decay, dt_bias, ld_proj, start, uint32_t(units), heads,
                          make_fastdiv(uint32_t(heads))};
-    // one thread per unit: blocks of kThreads threads = kThreads / 32 warps
-    const int64_t warps = (units + 31) / 32;
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(qdc::delta_gates), qdc::kThreads / 32, warps);
+    // one thread per unit
+    const int grid = grid_for(qdc::kThreads, units);
     return launch(ctx, qdc::delta_gates, grid, a, stream, "delta_gates");
 }
 
@@ -791,12 +752,12 @@ int conv_impl(qdc_ctx* ctx, float* q_out, float* k_out, float* v_out, int64_t v_
                     uint32_t(vec ? runs * per_tok : 0), make_fastdiv(uint32_t(per_tok)), seq_div, v_tok};
     if (vec) {
         auto k = qdc::delta_conv_norm_vec<R>;
-        const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32,
+        const int grid = grid_for(qdc::kThreads / 32,
                                   runs * per_tok);
         return launch(ctx, k, grid, a, stream, "delta_conv_norm");
     }
     auto k = qdc::delta_conv_norm_generic;
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, tokens * per_tok);
+    const int grid = grid_for(qdc::kThreads / 32, tokens * per_tok);
     return launch(ctx, k, grid, a, stream, "delta_conv_norm");
 }
 
@@ -868,7 +829,7 @@ int convert(qdc_ctx* ctx, void* out, const void* in, int64_t n, bool widen, void
     // (vector) or single elements
     int64_t items = vec ? (n / 8 + qdc::kConvertUnroll - 1) / qdc::kConvertUnroll : n;
     if (items < 1) items = 1;  // n < 8: the tail loop alone
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), kSmallThreads, items, kSmallThreads);
+    const int grid = grid_for(kSmallThreads, items);
     qdc::ConvertArgs a{out, in, n};
     return launch(ctx, k, grid, a, stream, widen ? "bf16_to_f32" : "f32_to_bf16", kSmallThreads);
 }
@@ -938,7 +899,7 @@ int qdc_swiglu(qdc_ctx* ctx, float* out_f32, uint16_t* out_bf16, const float* g,
         else if (out_f32) k = qdc::swiglu_vec<true, false>;
         else k = qdc::swiglu_vec<false, true>;
     }
-    const int grid = grid_for(ctx, reinterpret_cast<const void*>(k), qdc::kThreads / 32, rows);
+    const int grid = grid_for(qdc::kThreads / 32, rows);
     return launch(ctx, k, grid, a, stream, "swiglu");
 }
 

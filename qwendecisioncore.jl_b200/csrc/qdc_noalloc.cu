@@ -46,10 +46,9 @@
 static __device__ __align__(256) int32_t g_noalloc_ids[QDC_NOALLOC_MAX_IDS];
 
 // Defined in qdc_b200.cu (not exported): the per-thread text that
-// qdc_last_error(NULL) returns, the cached occupancy query and the grid rule.
+// qdc_last_error(NULL) returns and the grid rule.
 void qdc_set_thread_error(const char* msg);
-int qdc_resident_blocks(const void* kernel, int device, int threads);
-int64_t qdc_grid_size(int64_t cap, int64_t work_per_block_units, int64_t units);
+int64_t qdc_grid_size(int64_t work_per_block_units, int64_t units);
 
 namespace {
 
@@ -62,28 +61,25 @@ int noalloc_fail(int status, const char* msg, const char* detail = nullptr) {
 
 struct DeviceScratch {
     int32_t* ids = nullptr;
-    int sm_count = 0;
 };
 
 std::mutex g_setup_mu;
 DeviceScratch g_scratch[QDC_NOALLOC_MAX_DEVICES];
 
-// Device address of the id array and the SM count of `device`, looked up
-// once per device (the device must be current).
+// Device address of the id array on `device`, looked up once per device
+// (the device must be current).
 int setup(int device, DeviceScratch* out) {
     std::lock_guard<std::mutex> lock(g_setup_mu);
     DeviceScratch& s = g_scratch[device];
     if (s.ids == nullptr) {
-        int major = 0, sms = 0;
+        int major = 0;
         cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "cudaDeviceGetAttribute", cudaGetErrorString(e));
         if (major != 10) return noalloc_fail(QDC_EDEVICE, "libqdc_b200 is built for sm_100a");
         void* base = nullptr;
         e = cudaGetSymbolAddress(&base, g_noalloc_ids);
         if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "cudaGetSymbolAddress", cudaGetErrorString(e));
         s.ids = static_cast<int32_t*>(base);
-        s.sm_count = sms;
     }
     *out = s;
     return QDC_OK;
@@ -126,13 +122,11 @@ extern "C" int qdc_gather_rms_noalloc(void* out_x, void* out_y, const void* tabl
                      aligned16(gamma) && (hidden * esz) % 16 == 0;
     const qdc::RowKernel k = dtype == QDC_F32 ? qdc::row_kernel_for<float>(hidden, vec)
                                               : qdc::row_kernel_for<uint16_t>(hidden, vec);
-    // the context path's grid rule
-    const int64_t cap = int64_t(s.sm_count) *
-                        qdc_resident_blocks(reinterpret_cast<const void*>(k), device, qdc::kThreads);
-    const int64_t grid = qdc_grid_size(cap, qdc::kThreads / 32, n);
+    // the context path's grid rule and block size
+    const int64_t grid = qdc_grid_size(qdc::kSmallThreads / 32, n);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid));
-    cfg.blockDim = dim3(unsigned(qdc::kThreads));
+    cfg.blockDim = dim3(unsigned(qdc::kSmallThreads));
     cfg.stream = st;
     e = cudaLaunchKernelEx(&cfg, k, a);
     if (e != cudaSuccess) return noalloc_fail(QDC_ECUDA, "launch", cudaGetErrorString(e));

@@ -516,7 +516,15 @@ int launch_heads(qdc_ctx* ctx, const qdc::HeadArgs& a, bool vec_ok, void* stream
         if (!GATED) threads = kSmallThreads;
         units_per_block = int64_t(threads / 32) * (32 / lpu) * unroll;
     }
-    const int grid = grid_for(units_per_block, a.units);
+    int grid = grid_for(units_per_block, a.units);
+    // The q/k kernel moves 2 KB per unit; past ~41k blocks, block start-up
+    // costs more than a ragged end, so large launches give a warp several
+    // units (measured at 10 heads x 256: 65,536 tokens 1.007 of the copy
+    // peak with 4 units per warp against 0.974 with 1; 16,384 tokens, 1 unit
+    // per warp, 0.960 against 0.932 with 2).  The gated norm, row and SwiGLU
+    // kernels were fastest with one unit per warp step at every size.
+    constexpr int kQkMaxGrid = 40960;
+    if (!GATED && grid > kQkMaxGrid) grid = kQkMaxGrid;
     return launch(ctx, k, grid, a, stream, name, threads);
 }
 

@@ -127,6 +127,31 @@ __device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
     return __byte_perm(bf16_rounded(lo), bf16_rounded(hi), 0x7632);
 }
 
+// The same pair rounded by the hardware conversion: one instruction instead
+// of seven.  For every input that is not a NaN its bits equal bf16_pack's:
+// the integer rounding is round-to-nearest-even on the bit pattern, which for
+// finite values (subnormals included) and infinities is IEEE
+// round-to-nearest-even, the conversion's mode, overflow to infinity
+// included.  A NaN stays a NaN.  The integer rounding keeps a NaN's payload,
+// which is what the reference relies on for stored words, but a NaN that the
+// GPU's own arithmetic produced is the canonical 0x7fffffff, whose integer
+// rounding carries into the sign bit and stores -0.0, where the reference's
+// CPU arithmetic keeps a NaN.  So results of a kernel's own arithmetic that
+// may be NaN are rounded by this form.  It is not free: the conversion's
+// latency sits in front of the stores, and the bf16 row kernel measured 2%
+// slower with it on every value (gather + norm over 16,384 rows, 24.0
+// against 23.55 us), so that kernel keeps the integer form for rows without
+// a NaN; SwiGLU was level with it and uses it throughout.  qdc_f32_to_bf16,
+// which re-encodes stored words bit for bit, keeps bf16_pack.
+__device__ __forceinline__ uint32_t bf16_pack_cvt(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// One value by the hardware conversion: its bf16 bits in the low half.
+__device__ __forceinline__ uint32_t bf16_bits_cvt(float f) { return bf16_pack_cvt(f, 0.0f) & 0xffffu; }
+
 // A 16-byte chunk of a row (4 Float32 or 8 bf16 values) as loaded: the raw
 // bits stay packed in 4 registers while in flight and are widened to Float32
 // only when used, so bf16 rows keep as many bytes in flight per register as
@@ -144,6 +169,8 @@ template <> struct Chunk<float> {
     static __device__ __forceinline__ void store(float* p, const float (&v)[4]) {
         st_f4(p, make_float4(v[0], v[1], v[2], v[3]));
     }
+    static __device__ __forceinline__ void store_exact(float* p, const float (&v)[4]) { store(p, v); }
+    static __device__ __forceinline__ void store_nan_safe(float* p, const float (&v)[4]) { store(p, v); }
 };
 
 template <> struct Chunk<uint16_t> {
@@ -160,6 +187,20 @@ template <> struct Chunk<uint16_t> {
         st_u4(p, make_uint4(bf16_pack(v[0], v[1]), bf16_pack(v[2], v[3]),
                             bf16_pack(v[4], v[5]), bf16_pack(v[6], v[7])));
     }
+    // the same bits for every value that is not a NaN; a NaN stays a NaN
+    static __device__ __forceinline__ void store_nan_safe(uint16_t* p, const float (&v)[8]) {
+        st_u4(p, make_uint4(bf16_pack_cvt(v[0], v[1]), bf16_pack_cvt(v[2], v[3]),
+                            bf16_pack_cvt(v[4], v[5]), bf16_pack_cvt(v[6], v[7])));
+    }
+    // values that are widened bf16 words (low halves zero): their high
+    // halves, bit for bit, NaN payloads included
+    static __device__ __forceinline__ uint32_t hi_halves(float lo, float hi) {
+        return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+    }
+    static __device__ __forceinline__ void store_exact(uint16_t* p, const float (&v)[8]) {
+        st_u4(p, make_uint4(hi_halves(v[0], v[1]), hi_halves(v[2], v[3]),
+                            hi_halves(v[4], v[5]), hi_halves(v[6], v[7])));
+    }
 };
 
 template <typename T> __device__ __forceinline__ float scalar_load(const T* p);
@@ -170,7 +211,7 @@ template <> __device__ __forceinline__ float scalar_load<uint16_t>(const uint16_
 template <typename T> __device__ __forceinline__ void scalar_store(T* p, float v);
 template <> __device__ __forceinline__ void scalar_store<float>(float* p, float v) { *p = v; }
 template <> __device__ __forceinline__ void scalar_store<uint16_t>(uint16_t* p, float v) {
-    *p = uint16_t(bf16_bits(v));
+    *p = uint16_t(v == v ? bf16_bits(v) : bf16_bits_cvt(v));  // a NaN stays a NaN (bf16_pack_cvt)
 }
 
 // ------------------------------------------------------------------- math
@@ -332,6 +373,17 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
             }
             s = segment_sum<32>(s);
             const float scale = rms_scale(s, 1.0f / float(W), a.eps);
+            // bf16 rows whose results may hold a NaN round by the hardware
+            // conversion, so that a NaN stays a NaN (bf16_pack_cvt): r holds
+            // a NaN only if the sum of squares is NaN, and r * scale only if
+            // that sum or the scale is not finite (an infinite r, or eps 0
+            // with a zero row).  One warp-uniform test per row; the rest of
+            // the rows keep the cheaper integer rounding, and such a row is
+            // stored a second time after its integer-rounded stores (with a
+            // branch in front of the stores the gather + norm measured 3%
+            // slower).  A NaN or infinite gamma is not detected: its
+            // products round as integers.
+            const bool special = sizeof(T) == 2 && !bad[k] && !(s < INFINITY && scale < INFINITY);
             if (bad[k]) {
                 if (lane == 0 && a.flag) atomicOr(a.flag, 1);
 #pragma unroll
@@ -341,8 +393,20 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
             }
             if (a.out_r) {
                 T* rr = static_cast<T*>(a.out_r) + row * a.ld_r;
+                if (sizeof(T) == 2 && !a.m && !bad[k]) {
+                    // bf16, no add: r is x (the gathered row), copied bit for bit
 #pragma unroll
-                for (int c = 0; c < CHUNKS; ++c) C::store(rr + (c * 32 + lane) * N, v[c]);
+                    for (int c = 0; c < CHUNKS; ++c) C::store_exact(rr + (c * 32 + lane) * N, v[c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < CHUNKS; ++c) C::store(rr + (c * 32 + lane) * N, v[c]);
+                    // a bf16 row that may hold a NaN is stored again, NaN-safe;
+                    // the stores above do not wait for the reduction
+                    if (special) {
+#pragma unroll
+                        for (int c = 0; c < CHUNKS; ++c) C::store_nan_safe(rr + (c * 32 + lane) * N, v[c]);
+                    }
+                }
             }
             if (a.out_y) {
                 T* yr = static_cast<T*>(a.out_y) + row * a.ld_y;
@@ -362,6 +426,10 @@ __global__ void __launch_bounds__(kThreads) row_rms_vec(RowArgs a) {
                     for (int j = 0; j < N; ++j)
                         v[c][j] = bad[k] ? v[c][j] : __fmul_rn(__fmul_rn(v[c][j], scale), g[j]);
                     C::store(yr + (c * 32 + lane) * N, v[c]);
+                }
+                if (special) {  // stored again, NaN-safe
+#pragma unroll
+                    for (int c = 0; c < CHUNKS; ++c) C::store_nan_safe(yr + (c * 32 + lane) * N, v[c]);
                 }
             }
         }
@@ -397,7 +465,10 @@ __global__ void __launch_bounds__(kThreads) row_rms_generic(RowArgs a) {
             float r = scalar_load(xr + i);
             if (mr) r = __fadd_rn(r, scalar_load(mr + i));
             if (bad) r = __int_as_float(0x7fc00000);
-            if (rr) scalar_store(rr + i, r);
+            if (rr) {
+                if (mr || bad) scalar_store(rr + i, r);
+                else rr[i] = __ldg(xr + i);  // no add: r is x, copied bit for bit
+            }
             if (yr) {
                 const float g = a.centered ? __fadd_rn(1.0f, a.gamma[i]) : a.gamma[i];
                 scalar_store(yr + i, bad ? r : __fmul_rn(__fmul_rn(r, scale), g));
@@ -1238,7 +1309,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_vec(SwigluArgs a) {
                     if (F32) st_f4(a.out_f32 + row * a.ld_out + 4 * c, h);
                     if (BF16)
                         st_u2(a.out_bf16 + row * a.ld_out + 4 * c,
-                              make_uint2(bf16_pack(h.x, h.y), bf16_pack(h.z, h.w)));
+                              make_uint2(bf16_pack_cvt(h.x, h.y), bf16_pack_cvt(h.z, h.w)));
                 }
             }
         }
@@ -1256,7 +1327,7 @@ static __global__ void __launch_bounds__(kThreads) swiglu_generic(SwigluArgs a) 
             const float h = __fmul_rn(silu(__ldg(a.g + row * a.ld_g + i)),
                                       __ldg(a.u + row * a.ld_u + i));
             if (a.out_f32) a.out_f32[row * a.ld_out + i] = h;
-            if (a.out_bf16) a.out_bf16[row * a.ld_out + i] = uint16_t(bf16_bits(h));
+            if (a.out_bf16) a.out_bf16[row * a.ld_out + i] = uint16_t(bf16_bits_cvt(h));
         }
     }
 }

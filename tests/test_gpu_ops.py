@@ -180,6 +180,78 @@ def test_residual_rms_bf16(q, oracle, width):
     assert bf16_close(res, ex_r, oracle) and bf16_close(y, ex_y, oracle)
 
 
+def _bf16_bits(t):
+    return t.detach().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _f32_patterns(r, n):
+    """Float32 values that stress rounding to bf16: exact ties (low half
+    0x8000) on odd and even bf16 mantissas, one below and above a tie,
+    carries into the exponent, subnormals, the largest finites (overflow
+    to infinity), infinities, both signs, and random bit patterns."""
+    hi = r.integers(0, 0x7f80, n).astype(np.uint32) << 16
+    low = r.choice(np.array([0x8000, 0x7fff, 0x8001, 0xffff, 0x0000], np.uint32), n)
+    low = np.where(r.random(n) < 0.3, r.integers(0, 0x10000, n).astype(np.uint32), low)
+    bits = hi | low
+    k = n // 8
+    bits[:k] = r.integers(1, 0x800000, k).astype(np.uint32)  # subnormals
+    bits[k:k + 16] = 0x7f7fffff - np.arange(16, dtype=np.uint32) * 0x1000  # near the largest finite
+    bits[k + 16] = 0x7f800000  # infinity
+    bits |= (r.random(n) < 0.5).astype(np.uint32) << 31
+    return bits.view(np.float32)
+
+
+def test_bf16_row_store_rounding_is_bit_exact(q, oracle):
+    """The bf16 row kernel rounds its results by the reference's integer
+    rounding (src/safetensors.jl:38-42), and rows whose results may hold a
+    NaN (a non-finite sum of squares or scale) by the hardware conversion,
+    so that a NaN result stays a NaN (the integer rounding of the GPU's
+    canonical NaN would store -0.0).  Both must give the integer rounding's
+    bits for every value that is not a NaN.  A gathered row with no add is
+    copied bit for bit, NaN payloads included.
+
+    r = x + m over bf16 pairs a few exponents apart, so the Float32 sum has
+    bits below bf16 precision (ties, carries), checked bit for bit; one row
+    holds a NaN.  y: rows of r = +1 and -1 with eps 0 give a scale of
+    exactly 1, so y = +-gamma, and gamma runs over `_f32_patterns`
+    (subnormals, ties, overflow); a zero row beside them has an infinite
+    scale, so its y is NaN."""
+    r = rng(77)
+    rows, width = 512, 1024
+    xb = r.integers(0x0080, 0x7f00, (rows, width)).astype(np.uint16)
+    shift = r.integers(1, 12, (rows, width)).astype(np.uint16) << 7  # 1-11 binades lower
+    mb = np.where(xb > shift + 0x0080, xb - shift, xb).astype(np.uint16)
+    xb |= (r.random((rows, width)) < 0.5).astype(np.uint16) << 15
+    mb |= (r.random((rows, width)) < 0.5).astype(np.uint16) << 15
+    xb[0, :4] = [0x3f80, 0x3f81, 0xbf80, 0x3f80]  # 1 + 2^-8 and friends: exact ties
+    mb[0, :4] = [0x3b80, 0x3b80, 0xbb80, 0x3c00]
+    xb[1, 7] = 0x7fc0  # a NaN in row 1
+    w = r.normal(0, 0.02, width).astype(np.float32)
+    res, _ = q.native_residual_rms(dev_bf16(xb), dev_bf16(mb), dev(w), 1e-6)
+    exact = oracle.bf16_decode(xb) + oracle.bf16_decode(mb)  # IEEE Float32 sums
+    expected = oracle.bf16_encode(exact)
+    got = _bf16_bits(res)
+    keep = ~np.isnan(exact)
+    assert np.array_equal(got[keep], expected[keep])
+    assert np.isnan(oracle.bf16_decode(got[1, 7:8])).all()
+    ones = np.zeros((3, width), np.uint16)
+    ones[0], ones[1] = 0x3f80, 0xbf80  # rows of +1 and -1; row 2 stays zero
+    for launch in range(16):
+        g = _f32_patterns(rng(100 + launch), width)
+        _, y = q.native_residual_rms(dev_bf16(ones), None, dev(g), 0.0, centered=False)
+        got = _bf16_bits(y)
+        for row, sign in ((0, 1.0), (1, -1.0)):
+            want = oracle.bf16_encode((np.float32(sign) * g).astype(np.float32))
+            assert np.array_equal(got[row], want), (launch, row)
+        assert np.isnan(oracle.bf16_decode(got[2])).all()  # 0 x inf
+    # the gather alone: the table's words, NaN payloads and -0 included
+    table = r.integers(0, 0x10000, (64, width)).astype(np.uint16)
+    table[3, :4] = [0x7fc1, 0xffff, 0x7f81, 0x8000]
+    ids = np.array([3, 0, 63, 3, 17], np.int32)
+    x, _ = q.native_gather_rms(dev_bf16(table), ids, dev(w), 1e-6)
+    assert np.array_equal(_bf16_bits(x), table[ids])
+
+
 def test_rms_edge_values(q, oracle):
     x = np.zeros((4, 1024), np.float32)
     x[1] = 1e-30

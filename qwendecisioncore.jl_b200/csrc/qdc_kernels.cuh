@@ -976,21 +976,71 @@ __global__ void __launch_bounds__(kConvPipeThreads, 1) delta_conv_norm_pipe(Conv
             // its sequence -- one FMA chain per channel, no per-token branch.
             // The chain starts as fma(x, w, +0), like the reference's
             // `value = 0; value += x * w`, so a -0 product gives +0.
+            // Tokens go in groups of four, whose q/k sums of squares share
+            // one transposed butterfly (below).
+            static_assert(TPW % 4 == 0, "token groups of four");
 #pragma unroll
-            for (int r = 0; r < TPW; ++r) {
-                float4 acc;
-                acc.x = __fmaf_rn(xr[r].x, wt[0].x, 0.0f);
-                acc.y = __fmaf_rn(xr[r].y, wt[1].x, 0.0f);
-                acc.z = __fmaf_rn(xr[r].z, wt[2].x, 0.0f);
-                acc.w = __fmaf_rn(xr[r].w, wt[3].x, 0.0f);
+            for (int r0 = 0; r0 < TPW; r0 += 4) {
+                float4 acc[4];
 #pragma unroll
-                for (int j = 1; j < 4; ++j) {
-                    acc.x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc.x);
-                    acc.y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc.y);
-                    acc.z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc.z);
-                    acc.w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc.w);
+                for (int i = 0; i < 4; ++i) {
+                    const int r = r0 + i;
+                    acc[i].x = __fmaf_rn(xr[r].x, wt[0].x, 0.0f);
+                    acc[i].y = __fmaf_rn(xr[r].y, wt[1].x, 0.0f);
+                    acc[i].z = __fmaf_rn(xr[r].z, wt[2].x, 0.0f);
+                    acc[i].w = __fmaf_rn(xr[r].w, wt[3].x, 0.0f);
+#pragma unroll
+                    for (int j = 1; j < 4; ++j) {
+                        acc[i].x = __fmaf_rn(xr[r + j].x, (&wt[0].x)[j], acc[i].x);
+                        acc[i].y = __fmaf_rn(xr[r + j].y, (&wt[1].x)[j], acc[i].y);
+                        acc[i].z = __fmaf_rn(xr[r + j].z, (&wt[2].x)[j], acc[i].z);
+                        acc[i].w = __fmaf_rn(xr[r + j].w, (&wt[3].x)[j], acc[i].w);
+                    }
+                    acc[i].x = silu(acc[i].x);
+                    acc[i].y = silu(acc[i].y);
+                    acc[i].z = silu(acc[i].z);
+                    acc[i].w = silu(acc[i].w);
                 }
-                finish(r, acc);
+                if (h.group < 2) {
+                    // The four tokens' sums over the 32 lanes in one butterfly
+                    // whose first two levels each keep half of the sums: 6
+                    // shuffles and one rsqrt per lane instead of 20 and four,
+                    // then 4 shuffles bring each token's scale back.  Every
+                    // partial sum pairs the same lanes in the same order as
+                    // segment_sum<32>, so the totals are bit-identical.
+                    float s[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        s[i] = __fmul_rn(acc[i].x, acc[i].x);
+                        s[i] = __fmaf_rn(acc[i].y, acc[i].y, s[i]);
+                        s[i] = __fmaf_rn(acc[i].z, acc[i].z, s[i]);
+                        s[i] = __fmaf_rn(acc[i].w, acc[i].w, s[i]);
+                    }
+                    const bool hi16 = lane & 16, hi8 = lane & 8;
+                    // level 16: lanes 0-15 keep tokens 0 and 1, lanes 16-31 tokens 2 and 3
+                    float k0 = hi16 ? s[2] : s[0], k1 = hi16 ? s[3] : s[1];
+                    k0 += __shfl_xor_sync(kFull, hi16 ? s[0] : s[2], 16);
+                    k1 += __shfl_xor_sync(kFull, hi16 ? s[1] : s[3], 16);
+                    // level 8: of its pair, a lane keeps the first (bit 3 clear) or the second
+                    float t = hi8 ? k1 : k0;
+                    t += __shfl_xor_sync(kFull, hi8 ? k0 : k1, 8);
+                    t += __shfl_xor_sync(kFull, t, 4);
+                    t += __shfl_xor_sync(kFull, t, 2);
+                    t += __shfl_xor_sync(kFull, t, 1);
+                    // lane L now holds the total of token 2 (bit 4 of L) + (bit 3 of L)
+                    float sc = rsqrt_approx(__fadd_rn(t, a.eps));
+                    if (h.group == 0) sc = __fmul_rn(sc, a.q_inv_mult);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float scale = __shfl_sync(kFull, sc, ((i >> 1) << 4) | ((i & 1) << 3));
+                        acc[i].x = __fmul_rn(acc[i].x, scale);
+                        acc[i].y = __fmul_rn(acc[i].y, scale);
+                        acc[i].z = __fmul_rn(acc[i].z, scale);
+                        acc[i].w = __fmul_rn(acc[i].w, scale);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) st_f4(dst + (r0 + i) * dst_stride, acc[i]);
             }
         } else {
             int pos = pos0;

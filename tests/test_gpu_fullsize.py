@@ -138,3 +138,38 @@ def test_0p8b_delta_gates_16_heads(q, oracle):
     eb, ed = oracle.delta_gates(proj, start, 16, a_decay, dt_bias)
     gb, gd = q.native_delta_gates(dev(proj), start, 16, dev(a_decay), dev(dt_bias))
     assert close(gb, eb) and close(gd, ed)
+
+
+def test_grid_stride_loops_past_the_grid_cap(q, oracle):
+    """Grids stop where a loop's stride reaches 2^24 of the kernel's own
+    units, and larger launches loop.  The DeltaNet gates count their units
+    in 32 bits, one per thread: 2^24 + 4097 (token, head) units with one head
+    take the cap of 65,536 blocks of 256 threads, so 4,097 threads take a
+    second step of the grid-stride loop.  The residual
+    norm (64-bit rows) at width 32 over 2^24 + 1,237 rows takes the
+    4,194,304-block cap of its 4-row blocks; sampled rows are checked
+    (first, around each multiple of the stride, last)."""
+    rng = np.random.default_rng(24)
+    tokens = (1 << 24) + 4097
+    proj = rng.normal(0, 5, (tokens, 2)).astype(np.float32)
+    a_decay = np.array([-0.7], np.float32)
+    dt_bias = np.array([0.3], np.float32)
+    eb, ed = oracle.delta_gates(proj, 0, 1, a_decay, dt_bias)
+    gb, gd = q.native_delta_gates(dev(proj), 0, 1, dev(a_decay), dev(dt_bias))
+    assert close(gb, eb) and close(gd, ed)
+    del gb, gd, proj
+    rows, width = (1 << 24) + 1237, 32
+    g = torch.Generator(device="cuda")
+    g.manual_seed(24)
+    x = torch.randn((rows, width), generator=g, device="cuda")
+    m = torch.randn((rows, width), generator=g, device="cuda")
+    w = rng.normal(0, 0.02, width).astype(np.float32)
+    r, y = q.native_residual_rms(x, m, dev(w), 1e-6)
+    stride = (1 << 24) // 4 * 4  # rows per grid step: 4,194,304 blocks x 4 rows
+    pick = np.unique(np.concatenate([np.arange(0, 64), np.arange(stride - 64, min(stride + 64, rows)),
+                                     np.arange(rows - 64, rows),
+                                     rng.integers(0, rows, 512)]))
+    idx = torch.from_numpy(pick).cuda()
+    xs, ms = x[idx].cpu().numpy(), m[idx].cpu().numpy()
+    ex_r, ex_y = oracle.residual_rms(xs, ms, w, 1e-6)
+    assert np.array_equal(r[idx].cpu().numpy(), ex_r) and close(y[idx], ex_y)

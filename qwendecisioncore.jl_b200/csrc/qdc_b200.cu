@@ -140,8 +140,10 @@ int launch(qdc_ctx* ctx, void (*kernel)(Args), int grid, const Args& args, void*
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = ctx->pdl ? attr : nullptr;
     cfg.numAttrs = ctx->pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args);
-    if (e == cudaSuccess) e = cudaGetLastError();
+    // cudaLaunchKernelEx returns this launch's own error; the thread's
+    // last-error state (which may hold another library's pending error) is
+    // left to its owner
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args);
     if (e != cudaSuccess) return fail(ctx, QDC_ECUDA, "launch %s: %s", name, cudaGetErrorString(e));
     return QDC_OK;
 }

@@ -173,3 +173,18 @@ def test_grid_stride_loops_past_the_grid_cap(q, oracle):
     xs, ms = x[idx].cpu().numpy(), m[idx].cpu().numpy()
     ex_r, ex_y = oracle.residual_rms(xs, ms, w, 1e-6)
     assert np.array_equal(r[idx].cpu().numpy(), ex_r) and close(y[idx], ex_y)
+
+
+def test_residual_rms_bf16_32768_rows(q, oracle):
+    """The bf16-stored residual norm at the MLP-norm size (32,768 x 1,024):
+    r bit for bit against the oracle's integer rounding, y within 1e-2."""
+    rng = np.random.default_rng(32)
+    x = oracle.bf16_encode(rng.standard_normal((32768, 1024), dtype=np.float32))
+    m = oracle.bf16_encode(rng.standard_normal((32768, 1024), dtype=np.float32))
+    w = rng.standard_normal(1024, dtype=np.float32) * np.float32(0.02)
+    ex_r, ex_y = oracle.residual_rms_bf16(x, m, w, 1e-6)
+    b = lambda a: torch.from_numpy(a.view(np.int16)).cuda().view(torch.bfloat16)
+    r, y = q.native_residual_rms(b(x), b(m), dev(w), 1e-6)
+    bits = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(bits(r), ex_r)
+    assert close(oracle.bf16_decode(bits(y)), oracle.bf16_decode(ex_y), 1e-2)

@@ -244,6 +244,15 @@ def test_bf16_row_store_rounding_is_bit_exact(q, oracle):
             want = oracle.bf16_encode((np.float32(sign) * g).astype(np.float32))
             assert np.array_equal(got[row], want), (launch, row)
         assert np.isnan(oracle.bf16_decode(got[2])).all()  # 0 x inf
+    # the scalar kernel (width 40) rounds per value: the same bits, NaN kept
+    xs, ms = xb[:64, :40].copy(), mb[:64, :40].copy()
+    xs[5, 3] = 0xffc1  # a NaN
+    res40, _ = q.native_residual_rms(dev_bf16(xs), dev_bf16(ms), dev(w[:40]), 1e-6)
+    exact40 = oracle.bf16_decode(xs) + oracle.bf16_decode(ms)
+    got40 = _bf16_bits(res40)
+    keep40 = ~np.isnan(exact40)
+    assert np.array_equal(got40[keep40], oracle.bf16_encode(exact40)[keep40])
+    assert np.isnan(oracle.bf16_decode(got40[~keep40])).all()
     # the gather alone: the table's words, NaN payloads and -0 included
     table = r.integers(0, 0x10000, (64, width)).astype(np.uint16)
     table[3, :4] = [0x7fc1, 0xffff, 0x7f81, 0x8000]
